@@ -1,0 +1,144 @@
+// Fixed-point RMSNorm (rms_norm.py:10-60), optional fused residual add.
+// One CTA per row: 16-byte vector loads of x, the fp32 row (x + residual) is
+// kept in shared memory between the integer squared-sum and the scaling
+// pass, so x is read from HBM once and y written once.
+#include "fxp_common.cuh"
+
+namespace fxpr {
+
+template <int BITS, typename XT, int VEC>
+__global__ void __launch_bounds__(256) rms_norm_kernel(
+    const XT* __restrict__ x, int64_t xs, const void* __restrict__ w, int w_dtype,
+    void* __restrict__ y, int y_dtype, int64_t ys, void* __restrict__ res, int res_dtype,
+    int64_t rs, int64_t hidden, float eps, int frac) {
+  extern __shared__ float row_s[];
+  using UAcc = typename std::conditional<BITS == 64, unsigned long long, uint32_t>::type;
+  const int64_t row = blockIdx.x;
+  const XT* xr = x + row * xs;
+  const float scale = ldexpf(1.0f, frac);
+  UAcc acc = 0;
+
+  auto visit = [&](int64_t i, float v) {
+    if (res) {
+      v = __fadd_rn(v, load_f32(res, res_dtype, row * rs + i));  // rms_norm.py:43
+      store_f32(res, res_dtype, row * rs + i, v);                // rms_norm.py:44
+    }
+    row_s[i] = v;
+    acc += (UAcc)f2x_f32<BITS>(__fmul_rn(v, v), scale);         // rms_norm.py:46-51
+  };
+
+  if constexpr (VEC > 1) {
+    struct alignas(16) V { XT v[VEC]; };
+    const V* xv = reinterpret_cast<const V*>(xr);
+    const int64_t nv = hidden / VEC;
+    for (int64_t j = threadIdx.x; j < nv; j += blockDim.x) {
+      const V t = xv[j];
+#pragma unroll
+      for (int e = 0; e < VEC; ++e) visit(j * VEC + e, to_f32(t.v[e]));
+    }
+    for (int64_t i = nv * VEC + threadIdx.x; i < hidden; i += blockDim.x) visit(i, to_f32(xr[i]));
+  } else {
+    for (int64_t i = threadIdx.x; i < hidden; i += blockDim.x) visit(i, to_f32(xr[i]));
+  }
+
+  // exact integer block reduction (wraps like the reference's int32/int64 sum)
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+  __shared__ UAcc red[32];
+  __shared__ float rrms_s;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (lane == 0) red[warp] = acc;
+  __syncthreads();
+  if (warp == 0) {
+    acc = (lane < (int)(blockDim.x >> 5)) ? red[lane] : (UAcc)0;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+    if (lane == 0) {
+      // tl.sum of int16 F2X values accumulates in int32 (no 16-bit wrap)
+      float sum_f;
+      if constexpr (BITS == 64) {
+        sum_f = x2f_f32<64>((long long)acc, ldexpf(1.0f, -frac));
+      } else {
+        sum_f = x2f_f32<32>((int32_t)acc, ldexpf(1.0f, -frac));
+      }
+      const float mean = fmaxf(prim_div(sum_f, (float)hidden), 0.0f);  // rms_norm.py:56
+      rrms_s = prim_div(1.0f, prim_sqrt(__fadd_rn(mean, eps)));       // rms_norm.py:57
+    }
+  }
+  __syncthreads();
+  const float rrms = rrms_s;
+  for (int64_t i = threadIdx.x; i < hidden; i += blockDim.x) {
+    const float v = __fmul_rn(__fmul_rn(row_s[i], load_f32(w, w_dtype, i)), rrms);  // rms_norm.py:59
+    store_f32(y, y_dtype, row * ys + i, v);
+  }
+}
+
+template <int BITS, typename XT>
+static int launch_rms(const void* x, int64_t xs, const void* w, int w_dtype, void* y, int y_dtype,
+                      int64_t ys, void* res, int res_dtype, int64_t rs, int64_t rows, int64_t hidden,
+                      float eps, int frac, cudaStream_t st) {
+  constexpr int VEC = 16 / sizeof(XT);
+  const size_t smem = (size_t)hidden * sizeof(float);
+  const bool aligned = ((uintptr_t)x % 16 == 0) && ((xs * (int64_t)sizeof(XT)) % 16 == 0);
+  auto k = aligned ? rms_norm_kernel<BITS, XT, VEC> : rms_norm_kernel<BITS, XT, 1>;
+  if (smem > 48 * 1024) {
+    if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess) {
+      set_error("rms_norm_fxp: hidden size %lld too large", (long long)hidden);
+      return FXPR_ERR_INVALID;
+    }
+  }
+  k<<<(unsigned)rows, 256, smem, st>>>((const XT*)x, xs, w, w_dtype, y, y_dtype, ys, res, res_dtype,
+                                       rs, hidden, eps, frac);
+  return check_launch("fxpr_rms_norm_fxp");
+}
+
+template <int BITS>
+static int dispatch_rms(const void* x, int x_dtype, int64_t xs, const void* w, int w_dtype, void* y,
+                        int y_dtype, int64_t ys, void* res, int res_dtype, int64_t rs, int64_t rows,
+                        int64_t hidden, float eps, int frac, cudaStream_t st) {
+  switch (x_dtype) {
+    case FXPR_BF16:
+      return launch_rms<BITS, __nv_bfloat16>(x, xs, w, w_dtype, y, y_dtype, ys, res, res_dtype, rs,
+                                             rows, hidden, eps, frac, st);
+    case FXPR_F16:
+      return launch_rms<BITS, __half>(x, xs, w, w_dtype, y, y_dtype, ys, res, res_dtype, rs, rows,
+                                      hidden, eps, frac, st);
+    default:
+      return launch_rms<BITS, float>(x, xs, w, w_dtype, y, y_dtype, ys, res, res_dtype, rs, rows,
+                                     hidden, eps, frac, st);
+  }
+}
+
+}  // namespace fxpr
+
+using namespace fxpr;
+
+extern "C" int fxpr_rms_norm_fxp(const void* x, int x_dtype, int64_t x_row_stride, const void* w,
+                                 int w_dtype, void* y, int y_dtype, int64_t y_row_stride,
+                                 void* residual, int res_dtype, int64_t res_row_stride, int64_t rows,
+                                 int64_t hidden, float eps, int frac_bits, int int_bits,
+                                 void* stream) {
+  if (!valid_bits(int_bits)) {
+    set_error("fxp_int_bits must be 16/32/64, got %d", int_bits);
+    return FXPR_ERR_INVALID;
+  }
+  auto ok_f = [](int d) { return d == FXPR_F16 || d == FXPR_BF16 || d == FXPR_F32; };
+  if (!ok_f(x_dtype) || !ok_f(w_dtype) || !ok_f(y_dtype) || (residual && !ok_f(res_dtype))) {
+    set_error("rms_norm_fxp: tensors must be float16/bfloat16/float32");
+    return FXPR_ERR_INVALID;
+  }
+  if (rows <= 0 || hidden <= 0) return FXPR_OK;
+  if (rows > 0x7fffffffLL || hidden * 4 > 200 * 1024) {
+    set_error("rms_norm_fxp: shape too large (rows < 2^31, hidden <= 51200)");
+    return FXPR_ERR_INVALID;
+  }
+  const cudaStream_t st = (cudaStream_t)stream;
+  if (int_bits == 16)
+    return dispatch_rms<16>(x, x_dtype, x_row_stride, w, w_dtype, y, y_dtype, y_row_stride, residual,
+                            res_dtype, res_row_stride, rows, hidden, eps, frac_bits, st);
+  if (int_bits == 32)
+    return dispatch_rms<32>(x, x_dtype, x_row_stride, w, w_dtype, y, y_dtype, y_row_stride, residual,
+                            res_dtype, res_row_stride, rows, hidden, eps, frac_bits, st);
+  return dispatch_rms<64>(x, x_dtype, x_row_stride, w, w_dtype, y, y_dtype, y_row_stride, residual,
+                          res_dtype, res_row_stride, rows, hidden, eps, frac_bits, st);
+}
