@@ -1,0 +1,719 @@
+// Paged unified attention with fixed-point softmax (attention.py:18-489),
+// split-KV across a thread-block cluster with an exact integer combine.
+//
+// One CTA = (KV split s, KV head (slice of its query-head group), request,
+// tile of queries). Its rows are (query, head) pairs that share one KV head,
+// so every K/V element loaded from HBM is used by all rows of the group.
+//
+//   pass 1  K tiles (cp.async, 3 buffers) -> integer q.k per (row, key)
+//           -> fp32 score (X2F, scale, softcap, alibi, masks) kept in shared
+//           memory, row max over the split.
+//   DSMEM   row maxima exchanged across the cluster: global max per row,
+//           identical to the reference's whole-context pass 1.
+//   pass 2  V tiles -> p = exp2(score - max), integer normaliser and integer
+//           PV accumulation.
+//   DSMEM   integer partials summed across the cluster (exact, order-free),
+//           X2F, divide, store.
+// The result is bitwise independent of the split count and of the tiling.
+//
+// Products use the magic-constant RNE path when an exponent guard proves
+// |product * 2^f| < 2^22 for the whole tile; otherwise the exact
+// clamp-and-convert path of the reference runs for that tile.
+#include <cooperative_groups.h>
+
+#include "fxp_common.cuh"
+
+namespace cg = cooperative_groups;
+
+namespace fxpr {
+namespace attn {
+
+constexpr int THREADS = 256;
+constexpr int KT = 64;    // keys per tile
+constexpr int NBUF = 3;   // K/V tile buffers (two tiles in flight)
+constexpr int MAX_SPLITS = 8;
+
+struct Params {
+  const void* q;
+  int q_dtype;
+  int64_t q_st, q_sh;
+  const void* k;
+  const void* v;
+  int64_t k_sb, k_ss, k_sh;
+  int64_t v_sb, v_ss, v_sh;
+  void* o;
+  int o_dtype;
+  int64_t o_st, o_sh;
+  const int32_t* qsl;
+  const int32_t* seq_lens;
+  const int32_t* bt;
+  int64_t bt_stride;
+  const float* alibi;
+  int num_heads, num_kv_heads, group, gs, head_slices, qt, page;
+  int causal, window;
+  float scale_log2, softcap_log2;
+  int frac;
+  int exact_qk;  // q and K are 16-bit floats: products are exact in fp32
+  int cap;       // score capacity (keys) per CTA
+  int splits;
+  int qtiles;
+};
+
+// 16-byte chunk of KV elements -> fp32 pairs
+template <typename T> struct Chunk;
+template <> struct Chunk<__nv_bfloat16> {
+  static constexpr int E = 8;
+  __device__ static __forceinline__ void unpack(uint4 w, float2 (&out)[4]) {
+    const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+      out[i] = make_float2(__uint_as_float(ws[i] << 16), __uint_as_float(ws[i] & 0xFFFF0000u));
+  }
+};
+template <> struct Chunk<__half> {
+  static constexpr int E = 8;
+  __device__ static __forceinline__ void unpack(uint4 w, float2 (&out)[4]) {
+    const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) out[i] = __half22float2(*reinterpret_cast<const __half2*>(&ws[i]));
+  }
+};
+template <> struct Chunk<float> {
+  static constexpr int E = 4;
+  __device__ static __forceinline__ void unpack(uint4 w, float2 (&out)[2]) {
+    out[0] = make_float2(__uint_as_float(w.x), __uint_as_float(w.y));
+    out[1] = make_float2(__uint_as_float(w.z), __uint_as_float(w.w));
+  }
+};
+
+template <typename T> __device__ __forceinline__ uint32_t chunk_abs_or(uint4 w) {
+  return abs_or_as_f32<T>(w.x) | abs_or_as_f32<T>(w.y) | abs_or_as_f32<T>(w.z) |
+         abs_or_as_f32<T>(w.w);
+}
+
+// two V values -> fp32 after the reference's cast to fp16 (attention.py:245-249)
+template <typename T> __device__ __forceinline__ float2 v_pair_f16(const unsigned char* p);
+template <> __device__ __forceinline__ float2 v_pair_f16<__nv_bfloat16>(const unsigned char* p) {
+  const uint32_t w = *reinterpret_cast<const uint32_t*>(p);
+  const float a = __uint_as_float(w << 16), b = __uint_as_float(w & 0xFFFF0000u);
+  return __half22float2(__floats2half2_rn(a, b));
+}
+template <> __device__ __forceinline__ float2 v_pair_f16<__half>(const unsigned char* p) {
+  return __half22float2(*reinterpret_cast<const __half2*>(p));
+}
+template <> __device__ __forceinline__ float2 v_pair_f16<float>(const unsigned char* p) {
+  const float2 f = *reinterpret_cast<const float2*>(p);
+  return __half22float2(__floats2half2_rn(f.x, f.y));
+}
+
+template <int D, int RP, typename KVT>
+struct Smem {
+  static constexpr int ROWB = D * (int)sizeof(KVT);  // bytes of one key row
+  static constexpr int NC = ROWB / 16;               // 16-byte chunks per key row
+  static constexpr int SWZ = (NC < 8 ? NC : 8) - 1;  // chunk swizzle mask
+  static constexpr int TILEB = KT * ROWB;
+  static constexpr size_t off_q = 0;
+  static constexpr size_t off_qraw = off_q + (size_t)RP * D * 4;
+  static constexpr size_t off_kv = off_qraw + (size_t)RP * D * 4;
+  static constexpr size_t off_p = off_kv + (size_t)NBUF * TILEB;
+  static constexpr size_t off_acc = off_p + (size_t)KT * RP * 8;
+  static constexpr size_t off_den = off_acc + (size_t)RP * D * 8;
+  static constexpr size_t off_stmp = off_den + (size_t)RP * 8;
+  static constexpr size_t off_s = off_stmp + (size_t)RP * KT * 4;
+  static size_t bytes(int cap) { return off_s + (size_t)RP * cap * 4; }
+};
+
+}  // namespace attn
+}  // namespace fxpr
+
+namespace fxpr {
+namespace attn {
+
+template <int D, int RP, int BITS, typename KVT>
+__global__ void __launch_bounds__(THREADS) attn_kernel(Params p) {
+  using SM = Smem<D, RP, KVT>;
+  constexpr int ROWB = SM::ROWB, NC = SM::NC, SWZ = SM::SWZ, TILEB = SM::TILEB;
+  constexpr int CE = Chunk<KVT>::E;  // elements per 16-byte chunk
+  constexpr int KG = 512 / D;         // PV key groups
+  constexpr int KPT = KT / KG;        // PV keys per thread per tile
+  constexpr int RPT = RP / 4;         // score rows finalised per thread
+  using UAcc = typename std::conditional<BITS == 64, unsigned long long, uint32_t>::type;
+  static_assert(NC % 4 == 0, "head_dim too small for the chunk mapping");
+  static_assert(KPT % 2 == 0 && KPT >= 2, "PV key pairs");
+
+  extern __shared__ __align__(16) unsigned char smem[];
+  float* q_s = reinterpret_cast<float*>(smem + SM::off_q);
+  float* q_raw = reinterpret_cast<float*>(smem + SM::off_qraw);
+  unsigned char* kvbuf = smem + SM::off_kv;
+  float2* P2 = reinterpret_cast<float2*>(smem + SM::off_p);
+  unsigned long long* acc_s = reinterpret_cast<unsigned long long*>(smem + SM::off_acc);
+  unsigned long long* den_s = reinterpret_cast<unsigned long long*>(smem + SM::off_den);
+  float* S_tmp = reinterpret_cast<float*>(smem + SM::off_stmp);
+  float* S = reinterpret_cast<float*>(smem + SM::off_s);
+
+  __shared__ int row_tok[RP], row_head[RP], row_pos[RP], row_kend[RP];
+  __shared__ uint32_t gor[3];
+  __shared__ uint32_t gk, q_or;
+  __shared__ float wmax[THREADS / 32][RP];
+  __shared__ float rmax_s[RP], gmax_s[RP];
+
+  cg::cluster_group cluster = cg::this_cluster();
+  const int rank = (int)cluster.block_rank();
+  const int nsplit = p.splits;
+
+  const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
+  const int kvh = blockIdx.y / p.head_slices, hslice = blockIdx.y % p.head_slices;
+  const int req = blockIdx.z / p.qtiles, qtile = blockIdx.z % p.qtiles;
+  const int q_start = p.qsl[req], q_end = p.qsl[req + 1];
+  const int qlen = q_end - q_start;
+  const int seq_len = p.seq_lens[req];
+  const int ctx = seq_len - qlen;
+  if (qtile * p.qt >= qlen) return;  // uniform over the cluster (same y, z)
+  const float scale = ldexpf(1.0f, p.frac);
+  const float inv_scale = ldexpf(1.0f, -p.frac);
+
+  // ---- rows: (query, head) pairs of this CTA (attention.py:319-353) ----
+  if (t < RP) {
+    const int qi = t / p.gs, gh = t % p.gs;
+    const int qoff = qtile * p.qt + qi;
+    const int hg = hslice * p.gs + gh;
+    int tok = -1, kend = 0, pos = 0, head = 0;
+    if (qi < p.qt && qoff < qlen && hg < p.group) {
+      tok = q_start + qoff;
+      head = kvh * p.group + hg;
+      pos = ctx + qoff;
+      // the reference walks keys up to the end of its 64-row query block
+      kend = p.causal ? min(seq_len, ctx + (qoff / 64 + 1) * 64) : seq_len;
+    }
+    row_tok[t] = tok;
+    row_head[t] = head;
+    row_pos[t] = pos;
+    row_kend[t] = kend;
+  }
+  if (t < 3) gor[t] = 0u;
+  if (t == 0) {
+    gk = 0u;
+    q_or = 0u;
+  }
+  __syncthreads();
+  {
+    uint32_t qo = 0;
+    for (int e = t; e < RP * D; e += THREADS) {
+      const int i = e / D, d = e % D;
+      float v = 0.0f;
+      if (row_tok[i] >= 0)
+        v = load_f32(p.q, p.q_dtype, (int64_t)row_tok[i] * p.q_st + (int64_t)row_head[i] * p.q_sh + d);
+      q_raw[e] = v;
+      q_s[e] = __fmul_rn(v, scale);
+      qo |= __float_as_uint(v) & 0x7FFFFFFFu;
+      acc_s[e] = 0ull;
+    }
+    if (t < RP) den_s[t] = 0ull;
+    qo = __reduce_or_sync(0xffffffffu, qo);
+    if (lane == 0) atomicOr(&q_or, qo);
+  }
+  __syncthreads();
+
+  int kr_hi = 0;
+#pragma unroll
+  for (int i = 0; i < RP; ++i) kr_hi = max(kr_hi, row_kend[i]);
+  const int chunk = ((kr_hi + nsplit - 1) / nsplit + 15) & ~15;
+  const int kb = min(rank * chunk, kr_hi);
+  const int ke = min(kb + chunk, kr_hi);
+  const int ntiles = (ke - kb + KT - 1) / KT;
+  const int eq = exp_bound_f32(q_or);
+  const bool q_ok = eq + p.frac <= 126;
+  const int64_t bt_row = (int64_t)req * p.bt_stride;
+
+  // ---- tile copies: KT key rows of one KV head, 16-byte chunks, swizzled ----
+  auto issue = [&](const void* base, int64_t sb, int64_t ss, int64_t sh, int ti, int b) {
+    unsigned char* dst = kvbuf + b * TILEB;
+    const int k0 = kb + ti * KT;
+    for (int q = t; q < KT * NC; q += THREADS) {
+      const int jl = q / NC, c = q % NC;
+      const int j = k0 + jl;
+      int bytes = 0;
+      const unsigned char* src = reinterpret_cast<const unsigned char*>(base);
+      if (j < ke) {
+        const int64_t blk = p.bt[bt_row + j / p.page];
+        src += (blk * sb + (int64_t)(j % p.page) * ss + (int64_t)kvh * sh) * (int64_t)sizeof(KVT) + c * 16;
+        bytes = 16;
+      }
+      cp_async16(dst + jl * ROWB + ((c ^ (jl & SWZ)) * 16), src, bytes);
+    }
+  };
+  auto own_or = [&](int ti, int b) -> uint32_t {
+    const unsigned char* src = kvbuf + b * TILEB;
+    uint32_t o = 0;
+    for (int q = t; q < KT * NC; q += THREADS) {
+      const int jl = q / NC, c = q % NC;
+      if (kb + ti * KT + jl < ke)
+        o |= chunk_abs_or<KVT>(*reinterpret_cast<const uint4*>(src + jl * ROWB + ((c ^ (jl & SWZ)) * 16)));
+    }
+    return o;
+  };
+
+  // ---- scores of one K tile (attention.py:80-148) ----
+  // dst == nullptr: only the row max is updated (keys beyond the capacity)
+  float rmax[RPT];
+#pragma unroll
+  for (int u = 0; u < RPT; ++u) rmax[u] = -INFINITY;
+
+  auto qk_tile = [&](int ti, int b, bool fast, float* dst, int pitch, int col0, bool upd_max) {
+    const unsigned char* kt = kvbuf + b * TILEB;
+    const int jl = t >> 2, dq = t & 3;
+    const int j = kb + ti * KT + jl;
+    long long dot[RP];
+    if (fast) {
+      uint32_t acc[RP];
+#pragma unroll
+      for (int i = 0; i < RP; ++i) acc[i] = 0u;
+      const float2 C2 = make_float2(kMagic, kMagic);
+      auto body = [&](auto exact) {
+#pragma unroll 2
+        for (int rr = 0; rr < NC / 4; ++rr) {
+          const int c = rr * 4 + dq;
+          const uint4 w = *reinterpret_cast<const uint4*>(kt + jl * ROWB + ((c ^ (jl & SWZ)) * 16));
+          float2 kp[CE / 2];
+          Chunk<KVT>::unpack(w, kp);
+#pragma unroll
+          for (int i = 0; i < RP; ++i) {
+            const float* qrow = q_s + i * D + c * CE;
+#pragma unroll
+            for (int e = 0; e < CE / 2; e += 2) {
+              const float4 qv = *reinterpret_cast<const float4*>(qrow + 2 * e);
+              float2 r0, r1;
+              if constexpr (decltype(exact)::value) {
+                r0 = fma2(make_float2(qv.x, qv.y), kp[e], C2);
+                r1 = fma2(make_float2(qv.z, qv.w), kp[e + 1], C2);
+              } else {
+                r0 = add2(mul2(make_float2(qv.x, qv.y), kp[e]), C2);
+                r1 = add2(mul2(make_float2(qv.z, qv.w), kp[e + 1]), C2);
+              }
+              acc[i] += __float_as_uint(r0.x) + __float_as_uint(r0.y);
+              acc[i] += __float_as_uint(r1.x) + __float_as_uint(r1.y);
+            }
+          }
+        }
+      };
+      if (p.exact_qk) body(std::true_type{});
+      else body(std::false_type{});
+#pragma unroll
+      for (int i = 0; i < RP; ++i) {
+        acc[i] -= (uint32_t)(D / 4) * (uint32_t)kMagicBits;
+        dot[i] = (BITS == 64) ? (long long)(int32_t)acc[i] : (long long)acc[i];
+      }
+    } else {
+      // exact reference path: fp32 product, clamp, RNE convert, wrap
+      UAcc acc[RP];
+#pragma unroll
+      for (int i = 0; i < RP; ++i) acc[i] = 0;
+      for (int rr = 0; rr < NC / 4; ++rr) {
+        const int c = rr * 4 + dq;
+        const KVT* kv = reinterpret_cast<const KVT*>(kt + jl * ROWB + ((c ^ (jl & SWZ)) * 16));
+        for (int e = 0; e < CE; ++e) {
+          const float kf = to_f32(kv[e]);
+#pragma unroll
+          for (int i = 0; i < RP; ++i)
+            acc[i] += (UAcc)f2x_f32<BITS>(__fmul_rn(q_raw[i * D + c * CE + e], kf), scale);
+        }
+      }
+#pragma unroll
+      for (int i = 0; i < RP; ++i) dot[i] = (long long)acc[i];
+    }
+    // reduce over the 4 lanes that share the key
+#pragma unroll
+    for (int i = 0; i < RP; ++i) {
+      if constexpr (BITS == 64) {
+        dot[i] += __shfl_xor_sync(0xffffffffu, dot[i], 1);
+        dot[i] += __shfl_xor_sync(0xffffffffu, dot[i], 2);
+      } else {
+        uint32_t v = (uint32_t)dot[i];
+        v += __shfl_xor_sync(0xffffffffu, v, 1);
+        v += __shfl_xor_sync(0xffffffffu, v, 2);
+        dot[i] = (long long)(int32_t)v;
+      }
+    }
+    if (j >= ke) return;
+#pragma unroll
+    for (int u = 0; u < RPT; ++u) {
+      const int i = dq + 4 * u;
+      float s = -INFINITY;
+      if (j < row_kend[i]) {
+        float qk = (BITS == 64) ? __ll2float_rn(dot[i]) : __int2float_rn((int)dot[i]);
+        qk = __fmul_rn(__fmul_rn(qk, inv_scale), p.scale_log2);
+        if (p.softcap_log2 > 0.0f)
+          qk = __fmul_rn(p.softcap_log2, prim_tanh(prim_div(qk, p.softcap_log2)));
+        const int pos = row_pos[i];
+        if (p.alibi)
+          qk = __fadd_rn(qk, __fmul_rn(p.alibi[row_head[i]], __fsub_rn((float)j, (float)pos)));
+        bool ok = true;
+        if (p.causal) ok = ok && (pos >= j);
+        if (p.window > 0) ok = ok && (j > pos - p.window);
+        s = ok ? qk : -INFINITY;
+      }
+      if (dst) dst[i * pitch + col0 + jl] = s;
+      if (upd_max) rmax[u] = fmaxf(rmax[u], s);
+    }
+  };
+
+  // ================= pass 1: scores and row max =================
+  int g = 0;  // running tile counter: guard slot g % 3
+  issue(p.k, p.k_sb, p.k_ss, p.k_sh, 0, 0);
+  cp_async_commit();
+  if (1 < ntiles) issue(p.k, p.k_sb, p.k_ss, p.k_sh, 1, 1);
+  cp_async_commit();
+  for (int ti = 0; ti < ntiles; ++ti, ++g) {
+    const int b = ti % NBUF;
+    cp_async_wait<1>();
+    const uint32_t o = __reduce_or_sync(0xffffffffu, own_or(ti, b));
+    if (lane == 0) atomicOr(&gor[g % 3], o);
+    __syncthreads();
+    const int ek = exp_bound_f32(gor[g % 3]);
+    const bool fast = q_ok && (eq + ek + p.frac <= 22);
+    if (t == 0) gor[(g + 2) % 3] = 0u;
+    if (ti + 2 < ntiles) issue(p.k, p.k_sb, p.k_ss, p.k_sh, ti + 2, (ti + 2) % NBUF);
+    cp_async_commit();
+    const bool store = (ti + 1) * KT <= p.cap;
+    qk_tile(ti, b, fast, store ? S : nullptr, p.cap, ti * KT, true);
+  }
+  // row max over this split
+#pragma unroll
+  for (int u = 0; u < RPT; ++u) {
+    float m = rmax[u];
+    m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 4));
+    m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 8));
+    m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 16));
+    if (lane < 4) wmax[warp][lane + 4 * u] = m;
+  }
+  __syncthreads();  // also: every thread is done with the K buffers
+  if (t < RP) {
+    float m = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < THREADS / 32; ++w) m = fmaxf(m, wmax[w][t]);
+    rmax_s[t] = m;
+  }
+  // start streaming V while the maxima are exchanged
+  issue(p.v, p.v_sb, p.v_ss, p.v_sh, 0, 0);
+  cp_async_commit();
+  if (1 < ntiles) issue(p.v, p.v_sb, p.v_ss, p.v_sh, 1, 1);
+  cp_async_commit();
+  cluster.sync();
+  if (t < RP) {
+    float m = -INFINITY;
+    for (int q = 0; q < nsplit; ++q) m = fmaxf(m, *cluster.map_shared_rank(&rmax_s[t], q));
+    gmax_s[t] = m;  // == the reference's pass-1 max over the whole context
+  }
+  __syncthreads();
+
+  // ================= pass 2: normaliser and PV =================
+  const int prow = t % RP;  // p-phase row of this thread
+  UAcc den_acc = 0;
+  const int dp = t % (D / 2), kg = t / (D / 2);
+  const int vchunk = (2 * dp) / CE, vin = ((2 * dp) % CE) * (int)sizeof(KVT);
+  uint32_t accv[RP][2];
+  unsigned long long accv64[RP][2];
+#pragma unroll
+  for (int i = 0; i < RP; ++i) {
+    accv[i][0] = accv[i][1] = 0u;
+    accv64[i][0] = accv64[i][1] = 0ull;
+  }
+  const float2 C2 = make_float2(kMagic, kMagic);
+
+  for (int ti = 0; ti < ntiles; ++ti, ++g) {
+    const int b = ti % NBUF;
+    cp_async_wait<1>();
+    const uint32_t o = __reduce_or_sync(0xffffffffu, own_or(ti, b));
+    if (lane == 0) atomicOr(&gor[g % 3], o);
+    __syncthreads();
+    const int ev = exp_bound_f32(gor[g % 3]);
+    // |RN(p*v16) * 2^f| < 2^22 for p <= 1, and v finite in fp16
+    const bool fast = (ev + p.frac <= 21) && (ev <= 15);
+    if (t == 0) gor[(g + 2) % 3] = 0u;
+    const bool recompute = (ti + 1) * KT > p.cap;
+    if (recompute) {
+      // scores beyond the capacity: reload this K tile into the free buffer
+      const int kbuf = (ti + 2) % NBUF;
+      issue(p.k, p.k_sb, p.k_ss, p.k_sh, ti, kbuf);
+      cp_async_commit();
+      cp_async_wait<0>();
+      const uint32_t ko = __reduce_or_sync(0xffffffffu, own_or(ti, kbuf));
+      if (lane == 0) atomicOr(&gk, ko);
+      __syncthreads();
+      const int ek = exp_bound_f32(gk);
+      qk_tile(ti, kbuf, q_ok && (eq + ek + p.frac <= 22), S_tmp, KT, 0, false);
+      __syncthreads();
+      if (t == 0) gk = 0u;
+    }
+    if (ti + 2 < ntiles) issue(p.v, p.v_sb, p.v_ss, p.v_sh, ti + 2, (ti + 2) % NBUF);
+    cp_async_commit();
+
+    // p = exp2(score - max) (attention.py:237), normaliser (238-243)
+    const float gm = gmax_s[prow];
+    const int kend_p = row_kend[prow];
+    for (int jl = t / RP; jl < KT; jl += THREADS / RP) {
+      const int j = kb + ti * KT + jl;
+      float pv = 0.0f;
+      if (j < ke) {
+        const float sc = recompute ? S_tmp[prow * KT + jl] : S[prow * p.cap + ti * KT + jl];
+        pv = prim_exp2(__fsub_rn(sc, gm));
+        if (j < kend_p) den_acc += (UAcc)f2x_f32<BITS>(pv, scale);
+      }
+      const float ps = __fmul_rn(pv, scale);
+      P2[jl * RP + prow] = make_float2(ps, ps);
+    }
+    __syncthreads();
+
+    // PV (attention.py:245-255): acc[row][d] += F2X(p * fp16(v))
+    const unsigned char* vt = kvbuf + b * TILEB;
+    if (fast) {
+      uint32_t tv[RP][2];
+#pragma unroll
+      for (int i = 0; i < RP; ++i) tv[i][0] = tv[i][1] = 0u;
+#pragma unroll 2
+      for (int u = 0; u < KPT; u += 2) {
+        const int ja = kg + KG * u, jb = kg + KG * (u + 1);
+        const float2 va = v_pair_f16<KVT>(vt + ja * ROWB + ((vchunk ^ (ja & SWZ)) * 16) + vin);
+        const float2 vb = v_pair_f16<KVT>(vt + jb * ROWB + ((vchunk ^ (jb & SWZ)) * 16) + vin);
+#pragma unroll
+        for (int i = 0; i < RP; ++i) {
+          const float2 ra = add2(mul2(P2[ja * RP + i], va), C2);
+          const float2 rb = add2(mul2(P2[jb * RP + i], vb), C2);
+          tv[i][0] += __float_as_uint(ra.x) + __float_as_uint(rb.x);
+          tv[i][1] += __float_as_uint(ra.y) + __float_as_uint(rb.y);
+        }
+      }
+#pragma unroll
+      for (int i = 0; i < RP; ++i)
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const uint32_t v = tv[i][h] - (uint32_t)KPT * (uint32_t)kMagicBits;
+          if constexpr (BITS == 64) {
+            accv64[i][h] += (unsigned long long)(long long)(int32_t)v;
+          } else {
+            accv[i][h] += v;
+          }
+        }
+    } else {
+      for (int u = 0; u < KPT; ++u) {
+        const int jl = kg + KG * u;
+        const int j = kb + ti * KT + jl;
+        if (j >= ke) continue;
+        const float2 vv = v_pair_f16<KVT>(vt + jl * ROWB + ((vchunk ^ (jl & SWZ)) * 16) + vin);
+#pragma unroll
+        for (int i = 0; i < RP; ++i) {
+          if (j >= row_kend[i]) continue;
+          const float ps = P2[jl * RP + i].x;
+          const auto x0 = f2x_scaled<BITS>(__fmul_rn(ps, vv.x));
+          const auto x1 = f2x_scaled<BITS>(__fmul_rn(ps, vv.y));
+          if constexpr (BITS == 64) {
+            accv64[i][0] += (unsigned long long)x0;
+            accv64[i][1] += (unsigned long long)x1;
+          } else {
+            accv[i][0] += (uint32_t)x0;
+            accv[i][1] += (uint32_t)x1;
+          }
+        }
+      }
+    }
+  }
+  cp_async_wait<0>();
+
+  // ---- CTA partials (integer, exact) ----
+#pragma unroll
+  for (int i = 0; i < RP; ++i)
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const unsigned long long v = (BITS == 64) ? accv64[i][h] : (unsigned long long)accv[i][h];
+      if (v) atomicAdd(&acc_s[i * D + 2 * dp + h], v);
+    }
+  if (den_acc) atomicAdd(&den_s[prow], (unsigned long long)den_acc);
+  __syncthreads();
+  cluster.sync();
+
+  // ---- split combine across the cluster, finalize (attention.py:257-279) ----
+  for (int e = t; e < RP * D; e += THREADS) {
+    if (e % nsplit != rank) continue;
+    const int i = e / D, d = e % D;
+    if (row_tok[i] < 0) continue;
+    unsigned long long a = 0, dn = 0;
+    for (int q = 0; q < nsplit; ++q) {
+      a += *cluster.map_shared_rank(&acc_s[e], q);
+      dn += *cluster.map_shared_rank(&den_s[i], q);
+    }
+    float af, df;
+    if constexpr (BITS == 64) {
+      af = __fmul_rn(__ll2float_rn((long long)a), inv_scale);
+      df = __fmul_rn(__ll2float_rn((long long)dn), inv_scale);
+    } else {
+      af = __fmul_rn(__int2float_rn((int32_t)(uint32_t)a), inv_scale);
+      df = __fmul_rn(__int2float_rn((int32_t)(uint32_t)dn), inv_scale);
+    }
+    const float out = prim_div(af, fmaxf(df, 1.0e-6f));
+    store_f32(p.o, p.o_dtype, (int64_t)row_tok[i] * p.o_st + (int64_t)row_head[i] * p.o_sh + d, out);
+  }
+  cluster.sync();
+}
+
+// ---------------------------------------------------------------------------
+// host side
+// ---------------------------------------------------------------------------
+constexpr size_t kSmemBudget = 113 * 1024;  // two CTAs per SM
+
+template <int D, int RP, int BITS, typename KVT>
+static int launch(const Params& base, int max_keys, int splits, int req, int ys, cudaStream_t st) {
+  using SM = Smem<D, RP, KVT>;
+  Params p = base;
+  if (SM::off_s > kSmemBudget) {
+    set_error("unified_attention_fxp: head_dim/dtype combination exceeds shared memory");
+    return FXPR_ERR_UNSUPPORTED;
+  }
+  // score capacity: one split's keys when they fit the budget; keys beyond
+  // the capacity are rescored in pass 2
+  const int need = ((max_keys + splits - 1) / splits + 15) / 16 * 16 + 16;
+  int cap_max = (int)((kSmemBudget - SM::off_s) / (RP * 4)) / KT * KT;
+  int cap = (need + KT - 1) / KT * KT;
+  if (cap > cap_max) cap = cap_max;
+  p.cap = cap;
+  p.splits = splits;
+  const size_t smem = SM::bytes(cap);
+  auto k = attn_kernel<D, RP, BITS, KVT>;
+  static bool configured[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64 || !configured[dev]) {
+    if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBudget) !=
+        cudaSuccess) {
+      set_error("unified_attention_fxp: cannot configure shared memory");
+      return FXPR_ERR_CUDA;
+    }
+    if (dev >= 0 && dev < 64) configured[dev] = true;
+  }
+  const int64_t gz = (int64_t)req * p.qtiles;
+  if (gz > 65535) {
+    set_error("unified_attention_fxp: too many (request, query tile) pairs: %lld", (long long)gz);
+    return FXPR_ERR_UNSUPPORTED;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)splits, (unsigned)ys, (unsigned)gz);
+  cfg.blockDim = dim3(THREADS);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = (unsigned)splits;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, k, p);
+  if (e != cudaSuccess) {
+    set_error("unified_attention_fxp: launch failed: %s", cudaGetErrorString(e));
+    return FXPR_ERR_CUDA;
+  }
+  return check_launch("fxpr_unified_attention_fxp");
+}
+
+template <int D, int RP, int BITS>
+static int pick_kv(const Params& p, int kv_dtype, int max_keys, int splits, int req, int ys,
+                   cudaStream_t st) {
+  switch (kv_dtype) {
+    case FXPR_BF16: return launch<D, RP, BITS, __nv_bfloat16>(p, max_keys, splits, req, ys, st);
+    case FXPR_F16: return launch<D, RP, BITS, __half>(p, max_keys, splits, req, ys, st);
+    default:
+      if constexpr (D <= 128) {
+        return launch<D, RP, BITS, float>(p, max_keys, splits, req, ys, st);
+      } else {
+        set_error("unified_attention_fxp: float32 KV cache supports head_dim <= 128");
+        return FXPR_ERR_UNSUPPORTED;
+      }
+  }
+}
+
+template <int D>
+static int pick_rp(const Params& p, int rp, int bits, int kv_dtype, int max_keys, int splits,
+                   int req, int ys, cudaStream_t st) {
+  if (rp == 4) {
+    if (bits == 32) return pick_kv<D, 4, 32>(p, kv_dtype, max_keys, splits, req, ys, st);
+    return pick_kv<D, 4, 64>(p, kv_dtype, max_keys, splits, req, ys, st);
+  }
+  if (bits == 32) return pick_kv<D, 16, 32>(p, kv_dtype, max_keys, splits, req, ys, st);
+  return pick_kv<D, 16, 64>(p, kv_dtype, max_keys, splits, req, ys, st);
+}
+
+}  // namespace attn
+}  // namespace fxpr
+
+using namespace fxpr;
+
+extern "C" int fxpr_unified_attention_fxp(const fxpr_attention_params* a, void* stream) {
+  if (!a) {
+    set_error("unified_attention_fxp: null params");
+    return FXPR_ERR_INVALID;
+  }
+  if (a->int_bits == 16) {
+    set_error("unified_attention_fxp: int16 accumulators are not supported");
+    return FXPR_ERR_UNSUPPORTED;
+  }
+  if (a->int_bits != 32 && a->int_bits != 64) {
+    set_error("fxp_int_bits must be 16/32/64, got %d", a->int_bits);
+    return FXPR_ERR_INVALID;
+  }
+  const int D = a->head_dim;
+  if (D != 32 && D != 64 && D != 128 && D != 256) {
+    set_error("unified_attention_fxp: head_dim %d not supported (32/64/128/256)", D);
+    return FXPR_ERR_UNSUPPORTED;
+  }
+  auto okf = [](int d) { return d == FXPR_F16 || d == FXPR_BF16 || d == FXPR_F32; };
+  if (!okf(a->q_dtype) || !okf(a->kv_dtype) || !okf(a->o_dtype)) {
+    set_error("unified_attention_fxp: q/kv/o must be float16/bfloat16/float32");
+    return FXPR_ERR_UNSUPPORTED;
+  }
+  if (a->num_kv_heads <= 0 || a->num_heads % a->num_kv_heads != 0 || a->page_size <= 0) {
+    set_error("unified_attention_fxp: bad head counts or page size");
+    return FXPR_ERR_INVALID;
+  }
+  const int es = elem_size(a->kv_dtype);
+  const bool aligned = ((uintptr_t)a->k_cache % 16 == 0) && ((uintptr_t)a->v_cache % 16 == 0) &&
+                       ((a->k_stride_blk * es) % 16 == 0) && ((a->k_stride_slot * es) % 16 == 0) &&
+                       ((a->k_stride_head * es) % 16 == 0) && ((a->v_stride_blk * es) % 16 == 0) &&
+                       ((a->v_stride_slot * es) % 16 == 0) && ((a->v_stride_head * es) % 16 == 0);
+  if (!aligned) {
+    set_error("unified_attention_fxp: KV cache rows must be 16-byte aligned");
+    return FXPR_ERR_INVALID;
+  }
+  if (a->num_requests <= 0 || a->max_query_len <= 0) return FXPR_OK;
+  const int G = a->num_heads / a->num_kv_heads;
+  const int rp = (a->max_query_len == 1 && G <= 4) ? 4 : 16;
+  const int gs = G < rp ? G : rp;
+  attn::Params p = {};
+  p.q = a->q; p.q_dtype = a->q_dtype; p.q_st = a->q_stride_tok; p.q_sh = a->q_stride_head;
+  p.k = a->k_cache; p.v = a->v_cache;
+  p.k_sb = a->k_stride_blk; p.k_ss = a->k_stride_slot; p.k_sh = a->k_stride_head;
+  p.v_sb = a->v_stride_blk; p.v_ss = a->v_stride_slot; p.v_sh = a->v_stride_head;
+  p.o = a->o; p.o_dtype = a->o_dtype; p.o_st = a->o_stride_tok; p.o_sh = a->o_stride_head;
+  p.qsl = a->query_start_loc; p.seq_lens = a->seq_lens; p.bt = a->block_table;
+  p.bt_stride = a->bt_stride; p.alibi = a->alibi_slopes;
+  p.num_heads = a->num_heads; p.num_kv_heads = a->num_kv_heads; p.group = G; p.gs = gs;
+  p.head_slices = (G + gs - 1) / gs; p.qt = rp / gs; p.page = a->page_size;
+  p.causal = a->is_causal; p.window = a->window_size;
+  p.scale_log2 = a->scale_log2; p.softcap_log2 = a->logits_soft_cap;
+  p.frac = a->frac_bits;
+  p.exact_qk = (a->q_dtype != FXPR_F32) && (a->kv_dtype != FXPR_F32);
+  p.qtiles = (a->max_query_len + p.qt - 1) / p.qt;
+  int max_keys = a->max_seq_len > 0 ? a->max_seq_len : a->block_table_cols * a->page_size;
+  if (max_keys < 1) max_keys = 1;
+  int splits = a->num_kv_splits < 1 ? 1 : a->num_kv_splits;
+  if (splits > attn::MAX_SPLITS) splits = attn::MAX_SPLITS;
+  const int max_useful = (max_keys + attn::KT - 1) / attn::KT;  // no split shorter than a tile
+  if (splits > max_useful) splits = max_useful < 1 ? 1 : max_useful;
+  const int ys = a->num_kv_heads * p.head_slices;
+  const cudaStream_t st = (cudaStream_t)stream;
+  const int R = a->num_requests;
+  switch (D) {
+    case 32: return attn::pick_rp<32>(p, rp, a->int_bits, a->kv_dtype, max_keys, splits, R, ys, st);
+    case 64: return attn::pick_rp<64>(p, rp, a->int_bits, a->kv_dtype, max_keys, splits, R, ys, st);
+    case 128: return attn::pick_rp<128>(p, rp, a->int_bits, a->kv_dtype, max_keys, splits, R, ys, st);
+    default: return attn::pick_rp<256>(p, rp, a->int_bits, a->kv_dtype, max_keys, splits, R, ys, st);
+  }
+}

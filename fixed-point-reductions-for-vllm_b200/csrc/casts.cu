@@ -16,15 +16,17 @@ __device__ __forceinline__ long long f2x_any(const void* p, int dtype, int64_t i
   if (dtype == FXPR_F64) {
     const double x = reinterpret_cast<const double*>(p)[i];
     const double s = __dmul_rn(x, ldexp(1.0, frac));
-    const double c = fmin(fmax(s, qmin_of(BITS)), qmax_of(BITS, 53));
+    // the clamp constants are fp32 values (Triton materialises Python floats
+    // as fp32); out-of-range results saturate in the conversion
+    const double c = fmin(fmax(s, (double)(float)qmin_of(BITS)), (double)(float)qmax_of(BITS, 53));
     if (BITS == 64) return __double2ll_rn(c);
     return __double2int_rn(c);
   }
   if (dtype == FXPR_F16) {
     const __half x = reinterpret_cast<const __half*>(p)[i];
-    const __half s = __hmul(x, __double2half(ldexp(1.0, frac)));
-    const __half c =
-        __hmin(__hmax(s, __double2half(qmin_of(BITS))), __double2half(qmax_of(BITS, 11)));
+    const __half s = __hmul(x, __float2half_rn(ldexpf(1.0f, frac)));
+    const __half c = __hmin(__hmax(s, __float2half_rn((float)qmin_of(BITS))),
+                            __float2half_rn((float)qmax_of(BITS, 11)));
     if (BITS == 64) return __half2ll_rn(c);
     if (BITS == 16) return __half2short_rn(c);
     return __half2int_rn(c);

@@ -84,9 +84,12 @@ def float_to_fixed(x: torch.Tensor, frac_bits: int, int_bits: int) -> torch.Tens
         raise TypeError(f"x must be float16/float32/float64, got {x.dtype}")
     idt = int_dtype(int_bits)
     qmin_f, qmax_f = clamp_bounds(x.dtype, int_bits)
-    scale = torch.tensor(2.0**frac_bits, dtype=torch.float64).to(x.dtype)
-    qmin = torch.tensor(qmin_f, dtype=torch.float64).to(x.dtype)
-    qmax = torch.tensor(qmax_f, dtype=torch.float64).to(x.dtype)
+    # Triton materialises Python float constants as fp32 first, then casts
+    # them to x's dtype (for fp64 x, qmax 2^31-1 becomes 2^31 and the final
+    # conversion saturates).
+    scale = torch.tensor(2.0**frac_bits, dtype=torch.float32).to(x.dtype)
+    qmin = torch.tensor(qmin_f, dtype=torch.float32).to(x.dtype)
+    qmax = torch.tensor(qmax_f, dtype=torch.float32).to(x.dtype)
     scaled = x * scale
     nan = torch.isnan(scaled)
     clamped = torch.minimum(torch.maximum(scaled, qmin), qmax)
