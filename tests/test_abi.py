@@ -1,0 +1,95 @@
+"""The C-ABI library loads and exports every symbol include/fxpr_b200.h
+declares; argument validation runs on the host (no GPU needed)."""
+
+import ctypes
+import os
+import re
+
+import pytest
+import torch
+
+from fxpr_vllm import _native as N
+
+HEADER = os.path.join(os.path.dirname(os.path.dirname(__file__)), "include", "fxpr_b200.h")
+
+
+def header_symbols():
+    src = open(HEADER).read()
+    return sorted(set(re.findall(r"\b(fxpr_[a-z0-9_]+)\s*\(", src)))
+
+
+def test_library_exports_every_declared_symbol():
+    lib = N.load()
+    syms = header_symbols()
+    assert len(syms) >= 12
+    for s in syms:
+        assert hasattr(lib, s), s
+    assert set(syms) == set(N.EXPORTED)
+
+
+def test_abi_version():
+    assert N.load().fxpr_abi_version() == 1
+
+
+def test_invalid_bits_rejected_before_launch():
+    lib = N.load()
+    rc = lib.fxpr_float_to_fixed(None, N.F32, None, 24, 10, 16, None)
+    assert rc == N.FXPR_ERR_INVALID
+    assert "16/32/64" in lib.fxpr_last_error().decode()
+    with pytest.raises(ValueError):
+        N.check(rc, "float_to_fixed")
+
+
+def test_gemm_rejects_missing_workspace():
+    lib = N.load()
+    need = lib.fxpr_gemm_workspace_bytes(64, 4096, 4096, 32)
+    assert need > 0  # decode shapes use split-K
+    rc = lib.fxpr_gemm_fxp(None, N.BF16, 4096, 1, None, N.BF16, 4096, 1, None, 0, 4096, 1,
+                           64, 4096, 4096, 16, 32, None, 0, None)
+    assert rc == N.FXPR_ERR_INVALID
+    assert "workspace" in lib.fxpr_last_error().decode()
+
+
+def test_gemm_bad_frac_bits():
+    lib = N.load()
+    rc = lib.fxpr_gemm_fxp(None, N.BF16, 1, 1, None, N.BF16, 1, 1, None, 0, 1, 1,
+                           1, 1, 1, 40, 32, None, 0, None)
+    assert rc == N.FXPR_ERR_INVALID
+
+
+def test_attention_rejects_int16_and_bad_head_dim():
+    lib = N.load()
+    p = N.AttentionParams()
+    p.int_bits = 16
+    p.head_dim = 128
+    assert lib.fxpr_unified_attention_fxp(ctypes.byref(p), None) == N.FXPR_ERR_UNSUPPORTED
+    p.int_bits = 32
+    p.head_dim = 100
+    assert lib.fxpr_unified_attention_fxp(ctypes.byref(p), None) == N.FXPR_ERR_UNSUPPORTED
+
+
+def test_cpu_tensors_fail_loudly():
+    from fxpr_vllm.fixed_point_kernels import gemm
+
+    with pytest.raises(RuntimeError, match="CUDA"):
+        gemm.gemm_fxp(torch.zeros(2, 3), torch.zeros(3, 4), 16, 32)
+
+
+def test_library_ops_have_no_cpu_kernel():
+    import fxpr_vllm.library_ops  # noqa: F401
+
+    with pytest.raises(Exception):
+        torch.ops.fxpr.gemm_fxp(torch.zeros(2, 3), torch.zeros(3, 4), 16, 32)
+
+
+def test_fake_impls_shape():
+    import fxpr_vllm.library_ops  # noqa: F401
+    from torch._subclasses.fake_tensor import FakeTensorMode
+
+    with FakeTensorMode():
+        a = torch.empty(5, 7, device="cuda") if torch.cuda.is_available() else torch.empty(5, 7)
+        b = torch.empty(7, 3, device=a.device)
+        c = torch.ops.fxpr.gemm_fxp(a, b, 16, 32)
+        assert c.shape == (5, 3) and c.dtype == torch.float32
+        ci = torch.ops.fxpr.gemm_fxp_int(a, b, 16, 64)
+        assert ci.dtype == torch.int64
