@@ -161,7 +161,7 @@ __device__ __forceinline__ float prim_sqrt(float x) {
 }
 __device__ __forceinline__ float prim_tanh(float x) { return tanhf(x); }
 __device__ __forceinline__ float prim_exp(float x) { return __expf(x); }
-__device__ __forceinline__ float prim_log(float x) { return __logf(x); }
+__device__ __forceinline__ float prim_log(float x) { return logf(x); }
 
 // ---------------------------------------------------------------------------
 // packed fp32 pairs (sm_100 f32x2 arithmetic: one instruction, two lanes)

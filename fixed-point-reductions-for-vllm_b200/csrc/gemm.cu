@@ -503,8 +503,8 @@ extern "C" int fxpr_gemm_fxp(const void* a, int a_dtype, int64_t sam, int64_t sa
     set_error("gemm_fxp: a and b must be float16/bfloat16/float32");
     return FXPR_ERR_UNSUPPORTED;
   }
-  if (frac_bits < 0 || frac_bits >= int_bits) {
-    set_error("gemm_fxp: frac_bits must be in [0, %d), got %d", int_bits, frac_bits);
+  if (frac_bits < 0 || frac_bits > 100) {
+    set_error("gemm_fxp: frac_bits must be in [0, 100], got %d", frac_bits);
     return FXPR_ERR_INVALID;
   }
   if (out_kind != 0 && out_kind != 1) {

@@ -53,7 +53,7 @@ def test_gemm_rejects_missing_workspace():
 def test_gemm_bad_frac_bits():
     lib = N.load()
     rc = lib.fxpr_gemm_fxp(None, N.BF16, 1, 1, None, N.BF16, 1, 1, None, 0, 1, 1,
-                           1, 1, 1, 40, 32, None, 0, None)
+                           1, 1, 1, 200, 32, None, 0, None)
     assert rc == N.FXPR_ERR_INVALID
 
 
