@@ -86,9 +86,9 @@ template <> struct Chunk<float> {
   }
 };
 
-template <typename T> __device__ __forceinline__ uint32_t chunk_abs_or(uint4 w) {
-  return abs_or_as_f32<T>(w.x) | abs_or_as_f32<T>(w.y) | abs_or_as_f32<T>(w.z) |
-         abs_or_as_f32<T>(w.w);
+template <typename T> __device__ __forceinline__ uint32_t chunk_abs_max(uint4 w) {
+  return max(max(abs_max_as_f32<T>(w.x), abs_max_as_f32<T>(w.y)),
+             max(abs_max_as_f32<T>(w.z), abs_max_as_f32<T>(w.w)));
 }
 
 // two V values -> fp32 after the reference's cast to fp16 (attention.py:245-249)
@@ -205,12 +205,12 @@ __global__ void __launch_bounds__(THREADS) attn_kernel(Params p) {
         v = load_f32(p.q, p.q_dtype, (int64_t)row_tok[i] * p.q_st + (int64_t)row_head[i] * p.q_sh + d);
       q_raw[e] = v;
       q_s[e] = __fmul_rn(v, scale);
-      qo |= __float_as_uint(v) & 0x7FFFFFFFu;
+      qo = max(qo, __float_as_uint(v) & 0x7FFFFFFFu);
       acc_s[e] = 0ull;
     }
     if (t < RP) den_s[t] = 0ull;
-    qo = __reduce_or_sync(0xffffffffu, qo);
-    if (lane == 0) atomicOr(&q_or, qo);
+    qo = __reduce_max_sync(0xffffffffu, qo);
+    if (lane == 0) atomicMax(&q_or, qo);
   }
   __syncthreads();
 
@@ -221,8 +221,13 @@ __global__ void __launch_bounds__(THREADS) attn_kernel(Params p) {
   const int kb = min(rank * chunk, kr_hi);
   const int ke = min(kb + chunk, kr_hi);
   const int ntiles = (ke - kb + KT - 1) / KT;
-  const int eq = exp_bound_f32(q_or);
-  const bool q_ok = eq + p.frac <= 126;
+  const double scale_d = ldexp(1.0, p.frac);
+  const double mq = (double)__uint_as_float(q_or);
+  const bool q_ok = mq * scale_d < 3.0e38;
+  // exact magic-constant rounding of every q*k*2^f of a tile with max |k| = kmax
+  auto qk_fast = [&](uint32_t kmax) {
+    return q_ok && (mq * (double)__uint_as_float(kmax) * scale_d < 4194304.0);
+  };
   const int64_t bt_row = (int64_t)req * p.bt_stride;
 
   // ---- tile copies: KT key rows of one KV head, 16-byte chunks, swizzled ----
@@ -242,13 +247,13 @@ __global__ void __launch_bounds__(THREADS) attn_kernel(Params p) {
       cp_async16(dst + jl * ROWB + ((c ^ (jl & SWZ)) * 16), src, bytes);
     }
   };
-  auto own_or = [&](int ti, int b) -> uint32_t {
+  auto own_max = [&](int ti, int b) -> uint32_t {
     const unsigned char* src = kvbuf + b * TILEB;
     uint32_t o = 0;
     for (int q = t; q < KT * NC; q += THREADS) {
       const int jl = q / NC, c = q % NC;
       if (kb + ti * KT + jl < ke)
-        o |= chunk_abs_or<KVT>(*reinterpret_cast<const uint4*>(src + jl * ROWB + ((c ^ (jl & SWZ)) * 16)));
+        o = max(o, chunk_abs_max<KVT>(*reinterpret_cast<const uint4*>(src + jl * ROWB + ((c ^ (jl & SWZ)) * 16))));
     }
     return o;
   };
@@ -366,11 +371,10 @@ __global__ void __launch_bounds__(THREADS) attn_kernel(Params p) {
   for (int ti = 0; ti < ntiles; ++ti, ++g) {
     const int b = ti % NBUF;
     cp_async_wait<1>();
-    const uint32_t o = __reduce_or_sync(0xffffffffu, own_or(ti, b));
-    if (lane == 0) atomicOr(&gor[g % 3], o);
+    const uint32_t o = __reduce_max_sync(0xffffffffu, own_max(ti, b));
+    if (lane == 0) atomicMax(&gor[g % 3], o);
     __syncthreads();
-    const int ek = exp_bound_f32(gor[g % 3]);
-    const bool fast = q_ok && (eq + ek + p.frac <= 22);
+    const bool fast = qk_fast(gor[g % 3]);
     if (t == 0) gor[(g + 2) % 3] = 0u;
     if (ti + 2 < ntiles) issue(p.k, p.k_sb, p.k_ss, p.k_sh, ti + 2, (ti + 2) % NBUF);
     cp_async_commit();
@@ -423,12 +427,12 @@ __global__ void __launch_bounds__(THREADS) attn_kernel(Params p) {
   for (int ti = 0; ti < ntiles; ++ti, ++g) {
     const int b = ti % NBUF;
     cp_async_wait<1>();
-    const uint32_t o = __reduce_or_sync(0xffffffffu, own_or(ti, b));
-    if (lane == 0) atomicOr(&gor[g % 3], o);
+    const uint32_t o = __reduce_max_sync(0xffffffffu, own_max(ti, b));
+    if (lane == 0) atomicMax(&gor[g % 3], o);
     __syncthreads();
-    const int ev = exp_bound_f32(gor[g % 3]);
-    // |RN(p*v16) * 2^f| < 2^22 for p <= 1, and v finite in fp16
-    const bool fast = (ev + p.frac <= 21) && (ev <= 15);
+    // |RN(p * fp16(v)) * 2^f| < 2^22 for p <= 1, and fp16(v) finite
+    const double mv = (double)__uint_as_float(gor[g % 3]);
+    const bool fast = (mv <= 65504.0) && (mv * (1.0 + 1.0 / 1024) * scale_d < 4194304.0);
     if (t == 0) gor[(g + 2) % 3] = 0u;
     const bool recompute = (ti + 1) * KT > p.cap;
     if (recompute) {
@@ -437,11 +441,10 @@ __global__ void __launch_bounds__(THREADS) attn_kernel(Params p) {
       issue(p.k, p.k_sb, p.k_ss, p.k_sh, ti, kbuf);
       cp_async_commit();
       cp_async_wait<0>();
-      const uint32_t ko = __reduce_or_sync(0xffffffffu, own_or(ti, kbuf));
-      if (lane == 0) atomicOr(&gk, ko);
+      const uint32_t ko = __reduce_max_sync(0xffffffffu, own_max(ti, kbuf));
+      if (lane == 0) atomicMax(&gk, ko);
       __syncthreads();
-      const int ek = exp_bound_f32(gk);
-      qk_tile(ti, kbuf, q_ok && (eq + ek + p.frac <= 22), S_tmp, KT, 0, false);
+      qk_tile(ti, kbuf, qk_fast(gk), S_tmp, KT, 0, false);
       __syncthreads();
       if (t == 0) gk = 0u;
     }

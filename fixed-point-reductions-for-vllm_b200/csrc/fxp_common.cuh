@@ -201,23 +201,25 @@ template <int N> __device__ __forceinline__ void cp_async_wait() {
   asm volatile("cp.async.wait_group %0;\n" ::"n"(N));
 }
 
-// |x| < 2^E from an OR of absolute fp32 bit patterns (1000 for inf/NaN)
-__device__ __forceinline__ int exp_bound_f32(uint32_t o) {
-  const int e = (o >> 23) & 0xFF;
+// |x| < 2^E from the maximum absolute fp32 bit pattern of a set of values
+// (for non-negative floats the integer order of the patterns is the numeric
+// order, so an integer max gives the exact max magnitude); 1000 for inf/NaN.
+__device__ __forceinline__ int exp_bound_f32(uint32_t m) {
+  const int e = (m >> 23) & 0xFF;
   return e == 0xFF ? 1000 : (e == 0 ? -126 : e - 126);
 }
 
-// OR of the absolute values of the elements packed in a 32-bit word, as an
-// fp32 bit pattern with the same power-of-two bound
-template <typename T> __device__ __forceinline__ uint32_t abs_or_as_f32(uint32_t w);
-template <> __device__ __forceinline__ uint32_t abs_or_as_f32<float>(uint32_t w) {
+// max |x| over the elements packed in a 32-bit word, as an fp32 bit pattern
+// with the same power-of-two bound
+template <typename T> __device__ __forceinline__ uint32_t abs_max_as_f32(uint32_t w);
+template <> __device__ __forceinline__ uint32_t abs_max_as_f32<float>(uint32_t w) {
   return w & 0x7FFFFFFFu;
 }
-template <> __device__ __forceinline__ uint32_t abs_or_as_f32<__nv_bfloat16>(uint32_t w) {
-  return ((w & 0x7FFFu) | ((w >> 16) & 0x7FFFu)) << 16;
+template <> __device__ __forceinline__ uint32_t abs_max_as_f32<__nv_bfloat16>(uint32_t w) {
+  return max(w & 0x7FFFu, (w >> 16) & 0x7FFFu) << 16;
 }
-template <> __device__ __forceinline__ uint32_t abs_or_as_f32<__half>(uint32_t w) {
-  const uint32_t h = (w & 0x7FFFu) | ((w >> 16) & 0x7FFFu);
+template <> __device__ __forceinline__ uint32_t abs_max_as_f32<__half>(uint32_t w) {
+  const uint32_t h = max(w & 0x7FFFu, (w >> 16) & 0x7FFFu);
   const uint32_t e = (h >> 10) & 0x1F;
   if (e == 0x1F) return 0x7F800000u;
   if (e == 0) return h ? (uint32_t)(127 - 14) << 23 : 0u;  // subnormal: < 2^-14

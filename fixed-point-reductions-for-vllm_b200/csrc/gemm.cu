@@ -76,12 +76,12 @@ __global__ void __launch_bounds__(THREADS, MinBlocks<BITS>::v) gemm_kernel(Param
   constexpr int NRB = BLay<BT>::nrow_bytes;
   constexpr int KRB = BLay<BT>::krow_bytes;
   constexpr int EPC = 16 / (int)sizeof(BT);  // elements per 16-byte chunk
-  constexpr int LIM = (BITS == 16) ? 14 : 22;
+  constexpr double LIMV = (BITS == 16) ? 32767.5 : 4194304.0;
 
   extern __shared__ __align__(16) unsigned char smem[];
   unsigned char* bstage = smem;
   float* As = reinterpret_cast<float*>(smem + STAGES * SB);
-  __shared__ uint32_t gor[3][2];  // per-chunk OR of |A| and |B| bit patterns
+  __shared__ uint32_t gor[3][2];  // per-chunk max |A| and |B| bit patterns
   __shared__ int s_last;
 
   const int t = threadIdx.x, tx = t & 31, ty = t >> 5;
@@ -91,6 +91,7 @@ __global__ void __launch_bounds__(THREADS, MinBlocks<BITS>::v) gemm_kernel(Param
   const int64_t nchunks = cdiv(p.K, BK);
   const int64_t c0 = nchunks * split / p.splits, c1 = nchunks * (split + 1) / p.splits;
   const float scale = ldexpf(1.0f, p.frac);
+  const double scale_d = ldexp(1.0, p.frac);
   const BT* B = reinterpret_cast<const BT*>(p.b);
 
   if (t < 6) (&gor[0][0])[t] = 0u;
@@ -135,7 +136,7 @@ __global__ void __launch_bounds__(THREADS, MinBlocks<BITS>::v) gemm_kernel(Param
       }
     }
   };
-  // OR of |b| (as fp32 patterns) over the B elements this thread staged: its
+  // max |b| (as fp32 patterns) over the B elements this thread staged: its
   // own copies are visible to it after cp.async.wait_group
   auto own_b_or = [&](int s) -> uint32_t {
     const unsigned char* src = bstage + s * SB;
@@ -143,7 +144,7 @@ __global__ void __launch_bounds__(THREADS, MinBlocks<BITS>::v) gemm_kernel(Param
     if constexpr (LAYOUT == B_GENERIC) {
       for (int q = t; q < BK * BN; q += THREADS) {
         const int kr = q / BN, nn = q % BN;
-        o |= __float_as_uint(to_f32(reinterpret_cast<const BT*>(src + kr * NRB)[nn])) & 0x7FFFFFFFu;
+        o = max(o, __float_as_uint(to_f32(reinterpret_cast<const BT*>(src + kr * NRB)[nn])) & 0x7FFFFFFFu);
       }
     } else {
       constexpr int CPR = (LAYOUT == B_NCONTIG) ? BN / EPC : BK / EPC;
@@ -152,8 +153,8 @@ __global__ void __launch_bounds__(THREADS, MinBlocks<BITS>::v) gemm_kernel(Param
       for (int q = t; q < NCH; q += THREADS) {
         const int r = q / CPR, cc = q % CPR;
         const uint4 v = *reinterpret_cast<const uint4*>(src + r * RB + cc * 16);
-        o |= abs_or_as_f32<BT>(v.x) | abs_or_as_f32<BT>(v.y) | abs_or_as_f32<BT>(v.z) |
-             abs_or_as_f32<BT>(v.w);
+        o = max(o, max(max(abs_max_as_f32<BT>(v.x), abs_max_as_f32<BT>(v.y)),
+                     max(abs_max_as_f32<BT>(v.z), abs_max_as_f32<BT>(v.w))));
       }
     }
     return o;
@@ -176,7 +177,7 @@ __global__ void __launch_bounds__(THREADS, MinBlocks<BITS>::v) gemm_kernel(Param
     for (int r = 0; r < APT; ++r) {
       const int e = t + THREADS * r;
       dst[(e / BK) * A_LD + (e % BK)] = __fmul_rn(areg[r], scale);
-      o |= __float_as_uint(areg[r]) & 0x7FFFFFFFu;
+      o = max(o, __float_as_uint(areg[r]) & 0x7FFFFFFFu);
     }
     return o;
   };
@@ -253,16 +254,18 @@ __global__ void __launch_bounds__(THREADS, MinBlocks<BITS>::v) gemm_kernel(Param
     uint32_t aor = store_a(buf);
     cp_async_wait<STAGES - 2>();
     uint32_t bor = own_b_or(s);
-    aor = __reduce_or_sync(0xffffffffu, aor);
-    bor = __reduce_or_sync(0xffffffffu, bor);
+    aor = __reduce_max_sync(0xffffffffu, aor);
+    bor = __reduce_max_sync(0xffffffffu, bor);
     if (tx == 0) {
-      atomicOr(&gor[slot][0], aor);
-      atomicOr(&gor[slot][1], bor);
+      atomicMax(&gor[slot][0], aor);
+      atomicMax(&gor[slot][1], bor);
     }
     __syncthreads();
-    const int ea = exp_bound_f32(gor[slot][0]);
-    const int eb = exp_bound_f32(gor[slot][1]);
-    const bool fast = (ea + eb + p.frac <= LIM) && (ea + p.frac <= 126);
+    // fast path iff max|a| * max|b| * 2^f < 2^22 (32767.5 for int16): no
+    // saturation and an exact magic-constant rounding; NaN/inf compare false
+    const double ma = (double)__uint_as_float(gor[slot][0]);
+    const double mb = (double)__uint_as_float(gor[slot][1]);
+    const bool fast = (ma * mb * scale_d < LIMV) && (ma * scale_d < 3.0e38);
     if (t == 0) {
       // slot read two iterations ago; every thread has passed this barrier
       const int z = (int)((it + 2) % 3);
