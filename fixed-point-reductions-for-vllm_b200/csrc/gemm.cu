@@ -63,6 +63,7 @@ struct Params {
   int64_t tiles_n;
   void* ws;       // int32/int64 partial tiles
   int* counters;  // per-tile tickets
+  float one;      // 1.0f, opaque to the compiler (see the magic add below)
 };
 
 template <int BITS> struct MinBlocks { static constexpr int v = 2; };
@@ -162,11 +163,34 @@ __global__ void __launch_bounds__(THREADS, MinBlocks<BITS>::v) gemm_kernel(Param
 
   // ---- A staging through registers (converted to fp32, scaled by 2^f) ----
   float areg[APT];
+  // A elements of thread t: row (t*APT)/BK, k offset (t*APT)%BK .. +APT-1
+  const bool a_vec = (p.sak == 1) && (p.a_dtype == FXPR_BF16 || p.a_dtype == FXPR_F16) &&
+                     ((reinterpret_cast<uintptr_t>(p.a) & 15) == 0) && ((p.sam & 7) == 0);
   auto load_a = [&](int64_t c) {
+    const int e0 = t * APT;
+    const int64_t m = m0 + e0 / BK, k0 = c * BK + e0 % BK;
+    if constexpr (APT == 8) {
+      if (a_vec && m < p.M && k0 + 8 <= p.K) {
+        const uint4 w = *reinterpret_cast<const uint4*>(
+            reinterpret_cast<const char*>(p.a) + (m * p.sam + k0) * 2);
+        const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+        for (int h = 0; h < 4; ++h) {
+          if (p.a_dtype == FXPR_BF16) {
+            areg[2 * h] = __uint_as_float(ws[h] << 16);
+            areg[2 * h + 1] = __uint_as_float(ws[h] & 0xFFFF0000u);
+          } else {
+            const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&ws[h]));
+            areg[2 * h] = f.x;
+            areg[2 * h + 1] = f.y;
+          }
+        }
+        return;
+      }
+    }
 #pragma unroll
     for (int r = 0; r < APT; ++r) {
-      const int e = t + THREADS * r;
-      const int64_t m = m0 + e / BK, k = c * BK + e % BK;
+      const int64_t k = k0 + r;
       areg[r] = (m < p.M && k < p.K) ? load_f32(p.a, p.a_dtype, m * p.sam + k * p.sak) : 0.0f;
     }
   };
@@ -175,7 +199,7 @@ __global__ void __launch_bounds__(THREADS, MinBlocks<BITS>::v) gemm_kernel(Param
     uint32_t o = 0;
 #pragma unroll
     for (int r = 0; r < APT; ++r) {
-      const int e = t + THREADS * r;
+      const int e = t * APT + r;
       dst[(e / BK) * A_LD + (e % BK)] = __fmul_rn(areg[r], scale);
       o = max(o, __float_as_uint(areg[r]) & 0x7FFFFFFFu);
     }
@@ -281,6 +305,7 @@ __global__ void __launch_bounds__(THREADS, MinBlocks<BITS>::v) gemm_kernel(Param
     const unsigned char* Bb = bstage + s * SB;
     if (fast) {
       const float2 C2 = make_float2(kMagic, kMagic);
+      const float2 ONE2 = make_float2(p.one, p.one);
 #pragma unroll 2
       for (int kk = 0; kk < BK; kk += 4) {
         float2 bp[TN][2];
@@ -296,8 +321,10 @@ __global__ void __launch_bounds__(THREADS, MinBlocks<BITS>::v) gemm_kernel(Param
               r0 = fma2(a0, bp[j][0], C2);
               r1 = fma2(a1, bp[j][1], C2);
             } else {
-              r0 = add2(mul2(a0, bp[j][0]), C2);
-              r1 = add2(mul2(a1, bp[j][1]), C2);
+              // RN product, then the magic add as an FMA by a runtime 1.0:
+              // a plain add could be fused with the multiply into one rounding
+              r0 = fma2(mul2(a0, bp[j][0]), ONE2, C2);
+              r1 = fma2(mul2(a1, bp[j][1]), ONE2, C2);
             }
             acc[i][j] += __float_as_uint(r0.x) + __float_as_uint(r0.y);
             acc[i][j] += __float_as_uint(r1.x) + __float_as_uint(r1.y);
@@ -533,7 +560,7 @@ extern "C" int fxpr_gemm_fxp(const void* a, int a_dtype, int64_t sam, int64_t sa
   p.a = a; p.a_dtype = a_dtype; p.sam = sam; p.sak = sak;
   p.b = b; p.sbk = sbk; p.sbn = sbn;
   p.c = c; p.out_kind = out_kind; p.scm = scm; p.scn = scn;
-  p.M = M; p.N = N; p.K = K; p.frac = frac_bits;
+  p.M = M; p.N = N; p.K = K; p.frac = frac_bits; p.one = 1.0f;
   p.splits = pl.splits; p.tiles_n = pl.tiles_n;
   p.ws = workspace;
   p.counters = need > 0 ? reinterpret_cast<int*>(reinterpret_cast<char*>(workspace) + need -
