@@ -576,3 +576,85 @@ extern "C" int fxpr_gemm_fxp(const void* a, int a_dtype, int64_t sam, int64_t sa
   if (int_bits == 32) return gemm::pick_btype<64, 32>(p, b_dtype, pl.tiles, st);
   return gemm::pick_btype<64, 64>(p, b_dtype, pl.tiles, st);
 }
+
+// ---------------------------------------------------------------------------
+// Allocation-free variant of fxpr_gemm_fxp.
+//
+// Some callers cannot allocate device memory at the moment they run a GEMM:
+// for example an engine that plans every device buffer up front and forbids
+// allocation while serving, or a host binding (FFI from another language)
+// that has no device allocator of its own to hand a workspace to us. For
+// them the split-K workspace lives in a fixed array in this library's device
+// image instead of a caller-supplied buffer.
+//
+// The array is a host-side stand-in in host code, never a device address:
+// the device address is looked up once per device with cudaGetSymbolAddress
+// (with that device current) on the first call made on it, so that first call
+// should happen before any stream capture. Every call shares the one array,
+// so calls that overlap on the GPU (different streams, or several host
+// threads) race on it; serialise them. Each call zeroes the part it needs
+// before the launch.
+// ---------------------------------------------------------------------------
+namespace fxpr {
+namespace gemm {
+
+constexpr int64_t kNoAllocScratchBytes = 8ll << 20;  // 8 MiB per device
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
+
+static void* noalloc_scratch_ptr(int* rc) {
+  static void* ptrs[64] = {nullptr};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) {
+    set_error("gemm_fxp_noalloc: no current CUDA device");
+    *rc = FXPR_ERR_CUDA;
+    return nullptr;
+  }
+  if (ptrs[dev] == nullptr) {
+    void* p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess || p == nullptr) {
+      set_error("gemm_fxp_noalloc: cudaGetSymbolAddress failed: %s", cudaGetErrorString(e));
+      *rc = FXPR_ERR_CUDA;
+      return nullptr;
+    }
+    ptrs[dev] = p;
+  }
+  *rc = FXPR_OK;
+  return ptrs[dev];
+}
+
+}  // namespace gemm
+}  // namespace fxpr
+
+extern "C" int fxpr_gemm_fxp_noalloc(const void* a, int a_dtype, int64_t sam, int64_t sak,
+                                     const void* b, int b_dtype, int64_t sbk, int64_t sbn, void* c,
+                                     int out_kind, int64_t scm, int64_t scn, int64_t M, int64_t N,
+                                     int64_t K, int frac_bits, int int_bits, void* stream) {
+  if (!valid_bits(int_bits)) {
+    set_error("fxp_int_bits must be 16/32/64, got %d", int_bits);
+    return FXPR_ERR_INVALID;
+  }
+  if (M <= 0 || N <= 0) return fxpr_gemm_fxp(a, a_dtype, sam, sak, b, b_dtype, sbk, sbn, c, out_kind,
+                                             scm, scn, M, N, K, frac_bits, int_bits, nullptr, 0,
+                                             stream);
+  const int64_t need = fxpr_gemm_workspace_bytes(M, N, K, int_bits);
+  if (need > gemm::kNoAllocScratchBytes) {
+    set_error("gemm_fxp_noalloc: this shape needs %lld bytes of split-K scratch, above the "
+              "fixed %lld-byte maximum; use fxpr_gemm_fxp with a caller workspace",
+              (long long)need, (long long)gemm::kNoAllocScratchBytes);
+    return FXPR_ERR_INVALID;
+  }
+  void* ws = nullptr;
+  if (need > 0) {
+    int rc = FXPR_OK;
+    ws = gemm::noalloc_scratch_ptr(&rc);
+    if (rc != FXPR_OK) return rc;
+    const cudaError_t e = cudaMemsetAsync(ws, 0, (size_t)need, (cudaStream_t)stream);
+    if (e != cudaSuccess) {
+      set_error("gemm_fxp_noalloc: clearing the scratch failed: %s", cudaGetErrorString(e));
+      return FXPR_ERR_CUDA;
+    }
+  }
+  return fxpr_gemm_fxp(a, a_dtype, sam, sak, b, b_dtype, sbk, sbn, c, out_kind, scm, scn, M, N, K,
+                       frac_bits, int_bits, ws, need, stream);
+}

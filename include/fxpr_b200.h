@@ -79,6 +79,18 @@ int fxpr_gemm_fxp(const void* a, int a_dtype, int64_t sam, int64_t sak, const vo
                   int64_t scn, int64_t M, int64_t N, int64_t K, int frac_bits, int int_bits,
                   void* workspace, int64_t workspace_bytes, void* stream);
 
+/* Allocation-free fxpr_gemm_fxp for callers that cannot allocate device
+ * memory (a serving engine with a fixed, pre-planned memory budget, or a
+ * foreign-language binding with no device allocator). No counterpart in the
+ * reference. The split-K scratch is a fixed 8 MiB array inside the library,
+ * one per device; shapes needing more are rejected with FXPR_ERR_INVALID.
+ * The first call on a device looks the array up (make it before any stream
+ * capture); calls that overlap on the GPU share the array and race. */
+int fxpr_gemm_fxp_noalloc(const void* a, int a_dtype, int64_t sam, int64_t sak, const void* b,
+                          int b_dtype, int64_t sbk, int64_t sbn, void* c, int out_kind,
+                          int64_t scm, int64_t scn, int64_t M, int64_t N, int64_t K,
+                          int frac_bits, int int_bits, void* stream);
+
 /* Epilogue of a row-parallel linear layer after the integer allreduce:
  * out[m,n] = cast(X2F(acc[m,n]) + fp32(bias[n])) with acc int32 (int_bits 16:
  * low 16 bits, 32) or int64 (64); bias may be NULL; out_dtype F16/BF16/F32.
