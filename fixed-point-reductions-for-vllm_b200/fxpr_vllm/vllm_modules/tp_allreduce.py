@@ -1,0 +1,41 @@
+"""Integer allreduce of row-parallel fixed-point partials.
+
+The reference lets vLLM allreduce the *float* outputs of row-parallel layers
+(``RowParallelLinear.forward``, vllm/model_executor/layers/linear.py), which
+makes results depend on the TP degree. Here each rank produces its raw integer
+accumulator (``fxpr::gemm_fxp_int``), the accumulators are summed as int32 /
+int64 (exact and order-free, NCCL SUM over NVLink), and only then converted
+with X2F + bias + cast on every rank -- bitwise identical to TP=1.
+int16 accumulators travel as int32: the low 16 bits of a mod-2^32 sum are the
+mod-2^16 sum.
+"""
+
+from __future__ import annotations
+
+import torch
+import torch.distributed as dist
+
+
+def integer_all_reduce(t: torch.Tensor, group=None) -> torch.Tensor:
+    """Sum an int32/int64 tensor over a process group (exact). With
+    ``group=None`` the vLLM tensor-parallel group is used (its pynccl
+    communicator when available, which is CUDA-graph capturable)."""
+    if t.dtype not in (torch.int32, torch.int64):
+        raise TypeError(f"integer_all_reduce expects int32/int64, got {t.dtype}")
+    if group is not None:
+        if dist.get_world_size(group) > 1:
+            dist.all_reduce(t, op=dist.ReduceOp.SUM, group=group)
+        return t
+    from vllm.distributed import get_tp_group
+
+    tp = get_tp_group()
+    if tp.world_size == 1:
+        return t
+    comm = getattr(tp, "device_communicator", None)
+    pynccl = getattr(comm, "pynccl_comm", None) if comm is not None else None
+    if pynccl is not None and not getattr(pynccl, "disabled", True):
+        out = pynccl.all_reduce(t)
+        if out is not None:
+            return out
+    dist.all_reduce(t, op=dist.ReduceOp.SUM, group=tp.device_group)
+    return t
