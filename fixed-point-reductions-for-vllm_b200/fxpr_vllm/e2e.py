@@ -1,0 +1,159 @@
+"""End-to-end deterministic decode through vLLM with the fixed-point plugin.
+
+Builds a Llama-architecture checkpoint with seeded N(0, 0.02) weights on
+local disk (no network: no tokenizer, token-id prompts), then runs greedy
+decode with ``quantization="fixed_point_det"`` and
+``attention_backend="CUSTOM"``. Used by the GPU end-to-end test and as the
+decode tokens/s benchmark (BASELINE configs 4 and 5):
+
+    python -m fxpr_vllm.e2e --preset llama1b --prompts 32 --prompt-len 512 --gen 256 --tp 1
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import sys
+import time
+
+PRESETS = {
+    # ~1B Llama architecture
+    "llama1b": dict(hidden_size=2048, num_hidden_layers=16, num_attention_heads=32,
+                    num_key_value_heads=8, head_dim=64, intermediate_size=8192,
+                    rms_norm_eps=1e-5, rope_theta=500000.0, vocab_size=128256),
+    # Llama-3-8B architecture
+    "llama8b": dict(hidden_size=4096, num_hidden_layers=32, num_attention_heads=32,
+                    num_key_value_heads=8, head_dim=128, intermediate_size=14336,
+                    rms_norm_eps=1e-5, rope_theta=500000.0, vocab_size=128256),
+    # tiny model for tests
+    "tiny": dict(hidden_size=256, num_hidden_layers=2, num_attention_heads=8,
+                 num_key_value_heads=2, head_dim=32, intermediate_size=512,
+                 rms_norm_eps=1e-5, rope_theta=500000.0, vocab_size=1024),
+}
+
+
+def make_llama_dir(path: str, preset: str = "tiny", seed: int = 0) -> str:
+    """Write config.json + model.safetensors (bf16, weights N(0, 0.02), norms 1)."""
+    import torch
+    from safetensors.torch import save_file
+
+    cfg = dict(PRESETS[preset])
+    os.makedirs(path, exist_ok=True)
+    marker = os.path.join(path, "config.json")
+    if os.path.exists(marker) and os.path.exists(os.path.join(path, "model.safetensors")):
+        return path
+    conf = {
+        "architectures": ["LlamaForCausalLM"], "model_type": "llama", "torch_dtype": "bfloat16",
+        "hidden_act": "silu", "max_position_embeddings": 8192, "tie_word_embeddings": False,
+        "bos_token_id": 1, "eos_token_id": 2, "attention_bias": False, "mlp_bias": False,
+        **cfg,
+    }
+    g = torch.Generator().manual_seed(seed)
+    H, L, I, V = cfg["hidden_size"], cfg["num_hidden_layers"], cfg["intermediate_size"], cfg["vocab_size"]
+    nh, nkv, hd = cfg["num_attention_heads"], cfg["num_key_value_heads"], cfg["head_dim"]
+
+    def rnd(*shape):
+        return (torch.randn(*shape, generator=g) * 0.02).to(torch.bfloat16)
+
+    sd = {"model.embed_tokens.weight": rnd(V, H), "lm_head.weight": rnd(V, H),
+          "model.norm.weight": torch.ones(H, dtype=torch.bfloat16)}
+    for i in range(L):
+        p = f"model.layers.{i}."
+        sd[p + "self_attn.q_proj.weight"] = rnd(nh * hd, H)
+        sd[p + "self_attn.k_proj.weight"] = rnd(nkv * hd, H)
+        sd[p + "self_attn.v_proj.weight"] = rnd(nkv * hd, H)
+        sd[p + "self_attn.o_proj.weight"] = rnd(H, nh * hd)
+        sd[p + "mlp.gate_proj.weight"] = rnd(I, H)
+        sd[p + "mlp.up_proj.weight"] = rnd(I, H)
+        sd[p + "mlp.down_proj.weight"] = rnd(H, I)
+        sd[p + "input_layernorm.weight"] = torch.ones(H, dtype=torch.bfloat16)
+        sd[p + "post_attention_layernorm.weight"] = torch.ones(H, dtype=torch.bfloat16)
+    save_file(sd, os.path.join(path, "model.safetensors"))
+    with open(marker, "w") as f:
+        json.dump(conf, f)
+    return path
+
+
+def prompts(n: int, length: int, vocab: int, seed: int = 0) -> list[list[int]]:
+    import torch
+
+    g = torch.Generator().manual_seed(seed)
+    return torch.randint(3, vocab, (n, length), generator=g).tolist()
+
+
+def make_llm(model_dir: str, tp: int = 1, max_num_seqs: int = 256, gpu_mem: float = 0.5,
+             enforce_eager: bool = False, max_model_len: int = 4096):
+    pkg_root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    pp = os.environ.get("PYTHONPATH", "")
+    if pkg_root not in pp.split(os.pathsep):  # workers find the plugin entry point here
+        os.environ["PYTHONPATH"] = pkg_root + (os.pathsep + pp if pp else "")
+    if pkg_root not in sys.path:
+        sys.path.insert(0, pkg_root)
+    from fxpr_vllm.register import register
+
+    register()
+    from vllm import LLM
+
+    return LLM(model=model_dir, quantization="fixed_point_det", attention_backend="CUSTOM",
+               skip_tokenizer_init=True, tensor_parallel_size=tp, dtype="bfloat16",
+               max_num_seqs=max_num_seqs, gpu_memory_utilization=gpu_mem,
+               enforce_eager=enforce_eager, max_model_len=max_model_len, seed=0)
+
+
+def generate(llm, prompt_ids: list[list[int]], gen: int, batch: int | None = None):
+    """Greedy decode; ``batch`` splits the prompts into engine calls of that size."""
+    from vllm import SamplingParams
+    from vllm.inputs import TokensPrompt
+
+    sp = SamplingParams(temperature=0.0, max_tokens=gen, ignore_eos=True, detokenize=False)
+    outs = []
+    step = batch or len(prompt_ids)
+    for i in range(0, len(prompt_ids), step):
+        res = llm.generate([TokensPrompt(prompt_token_ids=p) for p in prompt_ids[i:i + step]], sp,
+                           use_tqdm=False)
+        outs.extend(list(r.outputs[0].token_ids) for r in res)
+    return outs
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--preset", default="llama1b", choices=sorted(PRESETS))
+    ap.add_argument("--model-dir", default=None)
+    ap.add_argument("--prompts", type=int, default=32)
+    ap.add_argument("--prompt-len", type=int, default=512)
+    ap.add_argument("--gen", type=int, default=256)
+    ap.add_argument("--tp", type=int, default=1)
+    ap.add_argument("--batches", default="", help="comma list of batch sizes to compare")
+    ap.add_argument("--out", default=None, help="write token streams (json) here")
+    args = ap.parse_args()
+    d = make_llama_dir(args.model_dir or f"/tmp/fxpr_{args.preset}", args.preset)
+    llm = make_llm(d, tp=args.tp, max_num_seqs=max(args.prompts, 1),
+                   max_model_len=args.prompt_len + args.gen + 16)
+    ps = prompts(args.prompts, args.prompt_len, PRESETS[args.preset]["vocab_size"])
+    generate(llm, ps[:2], 4)  # warm-up
+    # prefill-only pass to separate prefill time from decode time
+    t0 = time.perf_counter()
+    generate(llm, ps, 1)
+    t_prefill = time.perf_counter() - t0
+    t0 = time.perf_counter()
+    out = generate(llm, ps, args.gen)
+    t_all = time.perf_counter() - t0
+    decode_s = max(t_all - t_prefill, 1e-9)
+    res = {"preset": args.preset, "tp": args.tp, "prompts": args.prompts,
+           "prompt_len": args.prompt_len, "gen": args.gen,
+           "decode_tok_s": round(args.prompts * (args.gen - 1) / decode_s, 2),
+           "total_s": round(t_all, 3), "prefill_s": round(t_prefill, 3)}
+    if args.batches:
+        same = True
+        for b in [int(x) for x in args.batches.split(",")]:
+            same &= generate(llm, ps, args.gen, batch=b) == out
+        res["identical_across_batches"] = same
+    if args.out:
+        with open(args.out, "w") as f:
+            json.dump(out, f)
+    print(json.dumps(res), flush=True)
+
+
+if __name__ == "__main__":
+    main()
