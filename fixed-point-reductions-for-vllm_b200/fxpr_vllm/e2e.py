@@ -90,6 +90,9 @@ def make_llm(model_dir: str, tp: int = 1, max_num_seqs: int = 256, gpu_mem: floa
         os.environ["PYTHONPATH"] = pkg_root + (os.pathsep + pp if pp else "")
     if pkg_root not in sys.path:
         sys.path.insert(0, pkg_root)
+    # rendezvous on loopback: the host name of the box may not resolve
+    os.environ.setdefault("VLLM_HOST_IP", "127.0.0.1")
+    os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
     from fxpr_vllm.register import register
 
     register()
