@@ -57,6 +57,7 @@ struct Params {
   int cap;       // score capacity (keys) per CTA
   int splits;
   int qtiles;
+  int page_shift;  // log2(page) when page is a power of two, else -1
   float one;      // 1.0f, opaque to the compiler (magic add as an FMA)
 };
 
@@ -130,6 +131,25 @@ struct Smem {
 namespace fxpr {
 namespace attn {
 
+// Running max of |x| over raw 16-byte chunks / element pairs, kept as packed
+// 16-bit halves (bf16, fp16: one SIMD max per word) or as an fp32 pattern.
+template <typename T> __device__ __forceinline__ void absmax_word(uint32_t& m, uint32_t w) {
+  if constexpr (sizeof(T) == 2) {
+    m = __vmaxu2(m, w & 0x7FFF7FFFu);
+  } else {
+    m = max(m, w & 0x7FFFFFFFu);
+  }
+}
+// the running max as an fp32 value bounding |x| (inf/NaN stay non-finite)
+template <typename T> __device__ __forceinline__ float absmax_value(uint32_t m) {
+  if constexpr (sizeof(T) == 2) {
+    const uint32_t h = max(m & 0xFFFFu, m >> 16);
+    return __uint_as_float(abs_max_as_f32<T>(h));
+  } else {
+    return __uint_as_float(m);
+  }
+}
+
 template <int D, int RP, int BITS, typename KVT>
 __global__ void __launch_bounds__(THREADS) attn_kernel(Params p) {
   using SM = Smem<D, RP, KVT>;
@@ -138,8 +158,11 @@ __global__ void __launch_bounds__(THREADS) attn_kernel(Params p) {
   constexpr int KG = 512 / D;         // PV key groups
   constexpr int KPT = KT / KG;        // PV keys per thread per tile
   constexpr int RPT = RP / 4;         // score rows finalised per thread
+  constexpr int TPK = THREADS / KT;   // threads per key row in the copies
+  constexpr int CPT = NC / TPK;       // 16-byte chunks copied per thread
+  constexpr int RG = RP < 4 ? RP : 4; // rows per q-register group in the score loop
   using UAcc = typename std::conditional<BITS == 64, unsigned long long, uint32_t>::type;
-  static_assert(NC % 4 == 0, "head_dim too small for the chunk mapping");
+  static_assert(NC % 4 == 0 && NC % TPK == 0, "head_dim too small for the chunk mapping");
   static_assert(KPT % 2 == 0 && KPT >= 2, "PV key pairs");
 
   extern __shared__ __align__(16) unsigned char smem[];
@@ -153,8 +176,7 @@ __global__ void __launch_bounds__(THREADS) attn_kernel(Params p) {
   float* S = reinterpret_cast<float*>(smem + SM::off_s);
 
   __shared__ int row_tok[RP], row_head[RP], row_pos[RP], row_kend[RP];
-  __shared__ uint32_t gor[3];
-  __shared__ uint32_t gk, q_or;
+  __shared__ uint32_t q_or;
   __shared__ float wmax[THREADS / 32][RP];
   __shared__ float rmax_s[RP], gmax_s[RP];
 
@@ -191,11 +213,7 @@ __global__ void __launch_bounds__(THREADS) attn_kernel(Params p) {
     row_pos[t] = pos;
     row_kend[t] = kend;
   }
-  if (t < 3) gor[t] = 0u;
-  if (t == 0) {
-    gk = 0u;
-    q_or = 0u;
-  }
+  if (t == 0) q_or = 0u;
   __syncthreads();
   {
     uint32_t qo = 0;
@@ -222,41 +240,44 @@ __global__ void __launch_bounds__(THREADS) attn_kernel(Params p) {
   const int kb = min(rank * chunk, kr_hi);
   const int ke = min(kb + chunk, kr_hi);
   const int ntiles = (ke - kb + KT - 1) / KT;
-  const double scale_d = ldexp(1.0, p.frac);
-  const double mq = (double)__uint_as_float(q_or);
-  const bool q_ok = mq * scale_d < 3.0e38;
-  // exact magic-constant rounding of every q*k*2^f of a tile with max |k| = kmax
-  auto qk_fast = [&](uint32_t kmax) {
-    return q_ok && (mq * (double)__uint_as_float(kmax) * scale_d < 4194304.0);
-  };
   const int64_t bt_row = (int64_t)req * p.bt_stride;
 
-  // ---- tile copies: KT key rows of one KV head, 16-byte chunks, swizzled ----
+  // Per-thread fast-path thresholds (strict): a score product is exact through
+  // the magic constant iff max|q| * max|k| * 2^f < 2^22; a PV product iff
+  // max|v| <= 65504 (fp16 finite) and max|v| * (1 + 2^-10) * 2^f < 2^22.
+  // Rounded down to fp32 so the float compare is conservative.
+  const double scale_d = ldexp(1.0, p.frac);
+  const double mq = (double)__uint_as_float(q_or);
+  const bool q_ok = mq * scale_d < 3.0e38;  // q * 2^f finite (NaN: false)
+  const float kthr = q_ok ? __double2float_rd(4194304.0 / (mq * scale_d)) : 0.0f;
+  const float vthr = __double2float_rd(fmin(65504.5, 4194304.0 / (scale_d * (1.0 + 1.0 / 1024))));
+
+  // ---- tile copies: each thread copies CPT consecutive 16-byte chunks of
+  // one key row (one block-table lookup), XOR-swizzled in shared memory ----
   auto issue = [&](const void* base, int64_t sb, int64_t ss, int64_t sh, int ti, int b) {
-    unsigned char* dst = kvbuf + b * TILEB;
-    const int k0 = kb + ti * KT;
-    for (int q = t; q < KT * NC; q += THREADS) {
-      const int jl = q / NC, c = q % NC;
-      const int j = k0 + jl;
-      int bytes = 0;
-      const unsigned char* src = reinterpret_cast<const unsigned char*>(base);
-      if (j < ke) {
-        const int64_t blk = p.bt[bt_row + j / p.page];
-        src += (blk * sb + (int64_t)(j % p.page) * ss + (int64_t)kvh * sh) * (int64_t)sizeof(KVT) + c * 16;
-        bytes = 16;
+    const int jl = t / TPK, c0 = (t % TPK) * CPT;
+    const int j = kb + ti * KT + jl;
+    unsigned char* dst = kvbuf + b * TILEB + jl * ROWB;
+    const unsigned char* src = reinterpret_cast<const unsigned char*>(base);
+    int bytes = 0;
+    if (j < ke) {
+      int bi, slot;
+      if (p.page_shift >= 0) {
+        bi = j >> p.page_shift;
+        slot = j & (p.page - 1);
+      } else {
+        bi = j / p.page;
+        slot = j - bi * p.page;
       }
-      cp_async16(dst + jl * ROWB + ((c ^ (jl & SWZ)) * 16), src, bytes);
+      const int64_t blk = p.bt[bt_row + bi];
+      src += (blk * sb + (int64_t)slot * ss + (int64_t)kvh * sh) * (int64_t)sizeof(KVT);
+      bytes = 16;
     }
-  };
-  auto own_max = [&](int ti, int b) -> uint32_t {
-    const unsigned char* src = kvbuf + b * TILEB;
-    uint32_t o = 0;
-    for (int q = t; q < KT * NC; q += THREADS) {
-      const int jl = q / NC, c = q % NC;
-      if (kb + ti * KT + jl < ke)
-        o = max(o, chunk_abs_max<KVT>(*reinterpret_cast<const uint4*>(src + jl * ROWB + ((c ^ (jl & SWZ)) * 16))));
+#pragma unroll
+    for (int u = 0; u < CPT; ++u) {
+      const int c = c0 + u;
+      cp_async16(dst + ((c ^ (jl & SWZ)) * 16), src + c * 16, bytes);
     }
-    return o;
   };
 
   // ---- scores of one K tile (attention.py:80-148) ----
@@ -265,56 +286,68 @@ __global__ void __launch_bounds__(THREADS) attn_kernel(Params p) {
 #pragma unroll
   for (int u = 0; u < RPT; ++u) rmax[u] = -INFINITY;
 
-  auto qk_tile = [&](int ti, int b, bool fast, float* dst, int pitch, int col0, bool upd_max) {
+  auto qk_tile = [&](int ti, int b, float* dst, int pitch, int col0, bool upd_max) {
     const unsigned char* kt = kvbuf + b * TILEB;
     const int jl = t >> 2, dq = t & 3;
     const int j = kb + ti * KT + jl;
     long long dot[RP];
-    if (fast) {
-      uint32_t acc[RP];
+    uint32_t acc[RP];
 #pragma unroll
-      for (int i = 0; i < RP; ++i) acc[i] = 0u;
-      const float2 C2 = make_float2(kMagic, kMagic);
-      const float2 ONE2 = make_float2(p.one, p.one);
-      auto body = [&](auto exact) {
-#pragma unroll 2
-        for (int rr = 0; rr < NC / 4; ++rr) {
-          const int c = rr * 4 + dq;
-          const uint4 w = *reinterpret_cast<const uint4*>(kt + jl * ROWB + ((c ^ (jl & SWZ)) * 16));
-          float2 kp[CE / 2];
-          Chunk<KVT>::unpack(w, kp);
+    for (int i = 0; i < RP; ++i) acc[i] = 0u;
+    uint32_t km = 0;
+    const float2 C2 = make_float2(kMagic, kMagic);
+    const float2 ONE2 = make_float2(p.one, p.one);
+    auto body = [&](auto exact) {
 #pragma unroll
-          for (int i = 0; i < RP; ++i) {
-            const float* qrow = q_s + i * D + c * CE;
+      for (int rr = 0; rr < NC / 4; ++rr) {
+        const int c = rr * 4 + dq;
+        const uint4 w = *reinterpret_cast<const uint4*>(kt + jl * ROWB + ((c ^ (jl & SWZ)) * 16));
+        absmax_word<KVT>(km, w.x);
+        absmax_word<KVT>(km, w.y);
+        absmax_word<KVT>(km, w.z);
+        absmax_word<KVT>(km, w.w);
+        float2 kp[CE / 2];
+        Chunk<KVT>::unpack(w, kp);
 #pragma unroll
-            for (int e = 0; e < CE / 2; e += 2) {
-              const float4 qv = *reinterpret_cast<const float4*>(qrow + 2 * e);
+        for (int ig = 0; ig < RP; ig += RG) {
+          float4 qv[RG][CE / 4];  // q of RG rows for this chunk, loaded ahead of the math
+#pragma unroll
+          for (int r = 0; r < RG; ++r)
+#pragma unroll
+            for (int e = 0; e < CE / 4; ++e)
+              qv[r][e] = *reinterpret_cast<const float4*>(q_s + (ig + r) * D + c * CE + 4 * e);
+#pragma unroll
+          for (int r = 0; r < RG; ++r)
+#pragma unroll
+            for (int e = 0; e < CE / 4; ++e) {
               float2 r0, r1;
               if constexpr (decltype(exact)::value) {
-                r0 = fma2(make_float2(qv.x, qv.y), kp[e], C2);
-                r1 = fma2(make_float2(qv.z, qv.w), kp[e + 1], C2);
+                r0 = fma2(make_float2(qv[r][e].x, qv[r][e].y), kp[2 * e], C2);
+                r1 = fma2(make_float2(qv[r][e].z, qv[r][e].w), kp[2 * e + 1], C2);
               } else {
-                r0 = fma2(mul2(make_float2(qv.x, qv.y), kp[e]), ONE2, C2);
-                r1 = fma2(mul2(make_float2(qv.z, qv.w), kp[e + 1]), ONE2, C2);
+                r0 = fma2(mul2(make_float2(qv[r][e].x, qv[r][e].y), kp[2 * e]), ONE2, C2);
+                r1 = fma2(mul2(make_float2(qv[r][e].z, qv[r][e].w), kp[2 * e + 1]), ONE2, C2);
               }
-              acc[i] += __float_as_uint(r0.x) + __float_as_uint(r0.y);
-              acc[i] += __float_as_uint(r1.x) + __float_as_uint(r1.y);
+              acc[ig + r] += __float_as_uint(r0.x) + __float_as_uint(r0.y);
+              acc[ig + r] += __float_as_uint(r1.x) + __float_as_uint(r1.y);
             }
-          }
         }
-      };
-      if (p.exact_qk) body(std::true_type{});
-      else body(std::false_type{});
+      }
+    };
+    if (p.exact_qk) body(std::true_type{});
+    else body(std::false_type{});
+    if (absmax_value<KVT>(km) < kthr) {
 #pragma unroll
       for (int i = 0; i < RP; ++i) {
         acc[i] -= (uint32_t)(D / 4) * (uint32_t)kMagicBits;
         dot[i] = (BITS == 64) ? (long long)(int32_t)acc[i] : (long long)acc[i];
       }
     } else {
-      // exact reference path: fp32 product, clamp, RNE convert, wrap
-      UAcc acc[RP];
+      // this thread's keys hold values the magic constant cannot round
+      // exactly: redo its products on the exact reference path
+      UAcc ex[RP];
 #pragma unroll
-      for (int i = 0; i < RP; ++i) acc[i] = 0;
+      for (int i = 0; i < RP; ++i) ex[i] = 0;
       for (int rr = 0; rr < NC / 4; ++rr) {
         const int c = rr * 4 + dq;
         const KVT* kv = reinterpret_cast<const KVT*>(kt + jl * ROWB + ((c ^ (jl & SWZ)) * 16));
@@ -322,11 +355,11 @@ __global__ void __launch_bounds__(THREADS) attn_kernel(Params p) {
           const float kf = to_f32(kv[e]);
 #pragma unroll
           for (int i = 0; i < RP; ++i)
-            acc[i] += (UAcc)f2x_f32<BITS>(__fmul_rn(q_raw[i * D + c * CE + e], kf), scale);
+            ex[i] += (UAcc)f2x_f32<BITS>(__fmul_rn(q_raw[i * D + c * CE + e], kf), scale);
         }
       }
 #pragma unroll
-      for (int i = 0; i < RP; ++i) dot[i] = (long long)acc[i];
+      for (int i = 0; i < RP; ++i) dot[i] = (long long)ex[i];
     }
     // reduce over the 4 lanes that share the key
 #pragma unroll
@@ -369,23 +402,18 @@ __global__ void __launch_bounds__(THREADS) attn_kernel(Params p) {
   };
 
   // ================= pass 1: scores and row max =================
-  int g = 0;  // running tile counter: guard slot g % 3
   issue(p.k, p.k_sb, p.k_ss, p.k_sh, 0, 0);
   cp_async_commit();
   if (1 < ntiles) issue(p.k, p.k_sb, p.k_ss, p.k_sh, 1, 1);
   cp_async_commit();
-  for (int ti = 0; ti < ntiles; ++ti, ++g) {
+  for (int ti = 0; ti < ntiles; ++ti) {
     const int b = ti % NBUF;
     cp_async_wait<1>();
-    const uint32_t o = __reduce_max_sync(0xffffffffu, own_max(ti, b));
-    if (lane == 0) atomicMax(&gor[g % 3], o);
-    __syncthreads();
-    const bool fast = qk_fast(gor[g % 3]);
-    if (t == 0) gor[(g + 2) % 3] = 0u;
+    __syncthreads();  // tile ti visible to all; buffer (ti+2)%3 free
     if (ti + 2 < ntiles) issue(p.k, p.k_sb, p.k_ss, p.k_sh, ti + 2, (ti + 2) % NBUF);
     cp_async_commit();
     const bool store = (ti + 1) * KT <= p.cap;
-    qk_tile(ti, b, fast, store ? S : nullptr, p.cap, ti * KT, true);
+    qk_tile(ti, b, store ? S : nullptr, p.cap, ti * KT, true);
   }
   // row max over this split
 #pragma unroll
@@ -430,17 +458,28 @@ __global__ void __launch_bounds__(THREADS) attn_kernel(Params p) {
   }
   const float2 C2 = make_float2(kMagic, kMagic);
   const float2 ONE2 = make_float2(p.one, p.one);
+  // bf16 -> fp16 is exact for 2^-17 <= |v| <= 65504 (7 mantissa bits fit);
+  // smaller |v| give |p * v * 2^f| < 1/2 -> 0 either way when f <= 16
+  const bool v_exact16 = std::is_same<KVT, __nv_bfloat16>::value && p.frac <= 16;
 
-  for (int ti = 0; ti < ntiles; ++ti, ++g) {
+  // raw V pair of key jl at this thread's two dims
+  using VRaw = typename std::conditional<sizeof(KVT) == 2, uint32_t, uint2>::type;
+  auto v_raw = [&](const unsigned char* vt, int jl) -> VRaw {
+    return *reinterpret_cast<const VRaw*>(vt + jl * ROWB + ((vchunk ^ (jl & SWZ)) * 16) + vin);
+  };
+  auto v_f32 = [&](VRaw r) -> float2 {  // fp32(fp16(v)) as the reference computes it
+    if constexpr (sizeof(KVT) == 2) {
+      if (v_exact16) return make_float2(__uint_as_float(r << 16), __uint_as_float(r & 0xFFFF0000u));
+      return v_pair_f16<KVT>(reinterpret_cast<const unsigned char*>(&r));
+    } else {
+      return v_pair_f16<KVT>(reinterpret_cast<const unsigned char*>(&r));
+    }
+  };
+
+  for (int ti = 0; ti < ntiles; ++ti) {
     const int b = ti % NBUF;
     cp_async_wait<1>();
-    const uint32_t o = __reduce_max_sync(0xffffffffu, own_max(ti, b));
-    if (lane == 0) atomicMax(&gor[g % 3], o);
-    __syncthreads();
-    // |RN(p * fp16(v)) * 2^f| < 2^22 for p <= 1, and fp16(v) finite
-    const double mv = (double)__uint_as_float(gor[g % 3]);
-    const bool fast = (mv <= 65504.0) && (mv * (1.0 + 1.0 / 1024) * scale_d < 4194304.0);
-    if (t == 0) gor[(g + 2) % 3] = 0u;
+    __syncthreads();  // V tile ti visible; previous P2 consumed; buffer (ti+2)%3 free
     const bool recompute = (ti + 1) * KT > p.cap;
     if (recompute) {
       // scores beyond the capacity: reload this K tile into the free buffer
@@ -448,12 +487,9 @@ __global__ void __launch_bounds__(THREADS) attn_kernel(Params p) {
       issue(p.k, p.k_sb, p.k_ss, p.k_sh, ti, kbuf);
       cp_async_commit();
       cp_async_wait<0>();
-      const uint32_t ko = __reduce_max_sync(0xffffffffu, own_max(ti, kbuf));
-      if (lane == 0) atomicMax(&gk, ko);
       __syncthreads();
-      qk_tile(ti, kbuf, qk_fast(gk), S_tmp, KT, 0, false);
+      qk_tile(ti, kbuf, S_tmp, KT, 0, false);
       __syncthreads();
-      if (t == 0) gk = 0u;
     }
     if (ti + 2 < ntiles) issue(p.v, p.v_sb, p.v_ss, p.v_sh, ti + 2, (ti + 2) % NBUF);
     cp_async_commit();
@@ -474,58 +510,42 @@ __global__ void __launch_bounds__(THREADS) attn_kernel(Params p) {
     }
     __syncthreads();
 
-    // PV (attention.py:245-255): acc[row][d] += F2X(p * fp16(v))
+    // PV (attention.py:245-255): acc[row][d] += F2X(p * fp16(v)); optimistic
+    // magic-constant path, per-thread exact redo if its V values are too large
     const unsigned char* vt = kvbuf + b * TILEB;
-    // bf16 -> fp16 is exact for 2^-17 <= |v| <= 65504 (7 mantissa bits fit);
-    // smaller |v| give |p * v * 2^f| < 1/2 -> 0 either way when f <= 16
-    const bool v_exact16 = std::is_same<KVT, __nv_bfloat16>::value && p.frac <= 16;
-    if (fast && v_exact16) {
-      uint32_t tv[RP][2];
+    uint32_t tv[RP][2];
 #pragma unroll
-      for (int i = 0; i < RP; ++i) tv[i][0] = tv[i][1] = 0u;
+    for (int i = 0; i < RP; ++i) tv[i][0] = tv[i][1] = 0u;
+    uint32_t vm = 0;
 #pragma unroll 2
-      for (int u = 0; u < KPT; u += 2) {
-        const int ja = kg + KG * u, jb = kg + KG * (u + 1);
-        const uint32_t wa = *reinterpret_cast<const uint32_t*>(vt + ja * ROWB + ((vchunk ^ (ja & SWZ)) * 16) + vin);
-        const uint32_t wb = *reinterpret_cast<const uint32_t*>(vt + jb * ROWB + ((vchunk ^ (jb & SWZ)) * 16) + vin);
-        const float2 va = make_float2(__uint_as_float(wa << 16), __uint_as_float(wa & 0xFFFF0000u));
-        const float2 vb = make_float2(__uint_as_float(wb << 16), __uint_as_float(wb & 0xFFFF0000u));
+    for (int u = 0; u < KPT; u += 2) {
+      const int ja = kg + KG * u, jb = kg + KG * (u + 1);
+      const VRaw ra_ = v_raw(vt, ja), rb_ = v_raw(vt, jb);
+      float2 pa[RP], pb[RP];
 #pragma unroll
-        for (int i = 0; i < RP; ++i) {
-          const float2 ra = fma2(mul2(P2[ja * RP + i], va), ONE2, C2);
-          const float2 rb = fma2(mul2(P2[jb * RP + i], vb), ONE2, C2);
-          tv[i][0] += __float_as_uint(ra.x) + __float_as_uint(rb.x);
-          tv[i][1] += __float_as_uint(ra.y) + __float_as_uint(rb.y);
-        }
+      for (int i = 0; i < RP; ++i) {
+        pa[i] = P2[ja * RP + i];
+        pb[i] = P2[jb * RP + i];
       }
-#pragma unroll
-      for (int i = 0; i < RP; ++i)
-#pragma unroll
-        for (int h = 0; h < 2; ++h) {
-          const uint32_t v = tv[i][h] - (uint32_t)KPT * (uint32_t)kMagicBits;
-          if constexpr (BITS == 64) {
-            accv64[i][h] += (unsigned long long)(long long)(int32_t)v;
-          } else {
-            accv[i][h] += v;
-          }
-        }
-    } else if (fast) {
-      uint32_t tv[RP][2];
-#pragma unroll
-      for (int i = 0; i < RP; ++i) tv[i][0] = tv[i][1] = 0u;
-#pragma unroll 2
-      for (int u = 0; u < KPT; u += 2) {
-        const int ja = kg + KG * u, jb = kg + KG * (u + 1);
-        const float2 va = v_pair_f16<KVT>(vt + ja * ROWB + ((vchunk ^ (ja & SWZ)) * 16) + vin);
-        const float2 vb = v_pair_f16<KVT>(vt + jb * ROWB + ((vchunk ^ (jb & SWZ)) * 16) + vin);
-#pragma unroll
-        for (int i = 0; i < RP; ++i) {
-          const float2 ra = fma2(mul2(P2[ja * RP + i], va), ONE2, C2);
-          const float2 rb = fma2(mul2(P2[jb * RP + i], vb), ONE2, C2);
-          tv[i][0] += __float_as_uint(ra.x) + __float_as_uint(rb.x);
-          tv[i][1] += __float_as_uint(ra.y) + __float_as_uint(rb.y);
-        }
+      if constexpr (sizeof(KVT) == 2) {
+        absmax_word<KVT>(vm, ra_);
+        absmax_word<KVT>(vm, rb_);
+      } else {
+        absmax_word<KVT>(vm, ra_.x);
+        absmax_word<KVT>(vm, ra_.y);
+        absmax_word<KVT>(vm, rb_.x);
+        absmax_word<KVT>(vm, rb_.y);
       }
+      const float2 va = v_f32(ra_), vb = v_f32(rb_);
+#pragma unroll
+      for (int i = 0; i < RP; ++i) {
+        const float2 ra = fma2(mul2(pa[i], va), ONE2, C2);
+        const float2 rb = fma2(mul2(pb[i], vb), ONE2, C2);
+        tv[i][0] += __float_as_uint(ra.x) + __float_as_uint(rb.x);
+        tv[i][1] += __float_as_uint(ra.y) + __float_as_uint(rb.y);
+      }
+    }
+    if (absmax_value<KVT>(vm) < vthr) {
 #pragma unroll
       for (int i = 0; i < RP; ++i)
 #pragma unroll
@@ -745,6 +765,9 @@ extern "C" int fxpr_unified_attention_fxp(const fxpr_attention_params* a, void* 
   p.exact_qk = (a->q_dtype != FXPR_F32) && (a->kv_dtype != FXPR_F32);
   p.qtiles = (a->max_query_len + p.qt - 1) / p.qt;
   p.one = 1.0f;
+  p.page_shift = -1;
+  for (int sh = 0; sh < 31; ++sh)
+    if ((1 << sh) == a->page_size) p.page_shift = sh;
   int max_keys = a->max_seq_len > 0 ? a->max_seq_len : a->block_table_cols * a->page_size;
   if (max_keys < 1) max_keys = 1;
   int splits = a->num_kv_splits < 1 ? 1 : a->num_kv_splits;
