@@ -118,11 +118,11 @@ struct Smem {
   static constexpr size_t off_qraw = off_q + (size_t)RP * D * 4;
   static constexpr size_t off_kv = off_qraw + (size_t)RP * D * 4;
   static constexpr size_t off_p = off_kv + (size_t)NBUF * TILEB;
-  static constexpr size_t off_acc = off_p + (size_t)KT * RP * 8;
+  static constexpr size_t off_acc = off_p + (size_t)KT * RP * 4;
   static constexpr size_t off_den = off_acc + (size_t)RP * D * 8;
   static constexpr size_t off_stmp = off_den + (size_t)RP * 8;
   static constexpr size_t off_s = off_stmp + (size_t)RP * KT * 4;
-  static size_t bytes(int cap) { return off_s + (size_t)RP * cap * 4; }
+  static size_t bytes(int cap) { return off_s + (size_t)RP * (cap + 8) * 4; }
 };
 
 }  // namespace attn
@@ -163,13 +163,13 @@ __global__ void __launch_bounds__(THREADS) attn_kernel(Params p) {
   constexpr int RG = RP < 4 ? RP : 4; // rows per q-register group in the score loop
   using UAcc = typename std::conditional<BITS == 64, unsigned long long, uint32_t>::type;
   static_assert(NC % 4 == 0 && NC % TPK == 0, "head_dim too small for the chunk mapping");
-  static_assert(KPT % 2 == 0 && KPT >= 2, "PV key pairs");
+  static_assert(KPT % 4 == 0 && KPT >= 4, "PV key quads");
 
   extern __shared__ __align__(16) unsigned char smem[];
   float* q_s = reinterpret_cast<float*>(smem + SM::off_q);
   float* q_raw = reinterpret_cast<float*>(smem + SM::off_qraw);
   unsigned char* kvbuf = smem + SM::off_kv;
-  float2* P2 = reinterpret_cast<float2*>(smem + SM::off_p);
+  float* P = reinterpret_cast<float*>(smem + SM::off_p);  // [row][key slot], p * 2^f
   unsigned long long* acc_s = reinterpret_cast<unsigned long long*>(smem + SM::off_acc);
   unsigned long long* den_s = reinterpret_cast<unsigned long long*>(smem + SM::off_den);
   float* S_tmp = reinterpret_cast<float*>(smem + SM::off_stmp);
@@ -413,7 +413,7 @@ __global__ void __launch_bounds__(THREADS) attn_kernel(Params p) {
     if (ti + 2 < ntiles) issue(p.k, p.k_sb, p.k_ss, p.k_sh, ti + 2, (ti + 2) % NBUF);
     cp_async_commit();
     const bool store = (ti + 1) * KT <= p.cap;
-    qk_tile(ti, b, store ? S : nullptr, p.cap, ti * KT, true);
+    qk_tile(ti, b, store ? S : nullptr, p.cap + 8, ti * KT, true);
   }
   // row max over this split
 #pragma unroll
@@ -501,12 +501,12 @@ __global__ void __launch_bounds__(THREADS) attn_kernel(Params p) {
       const int j = kb + ti * KT + jl;
       float pv = 0.0f;
       if (j < ke) {
-        const float sc = recompute ? S_tmp[prow * KT + jl] : S[prow * p.cap + ti * KT + jl];
+        const float sc = recompute ? S_tmp[prow * KT + jl] : S[prow * (p.cap + 8) + ti * KT + jl];
         pv = prim_exp2(__fsub_rn(sc, gm));
         if (j < kend_p) den_acc += (UAcc)f2x_f32<BITS>(pv, scale);
       }
-      const float ps = __fmul_rn(pv, scale);
-      P2[jl * RP + prow] = make_float2(ps, ps);
+      // key slot: the KPT keys of PV thread group kg are contiguous
+      P[prow * KT + (jl % KG) * KPT + jl / KG] = __fmul_rn(pv, scale);
     }
     __syncthreads();
 
@@ -517,32 +517,37 @@ __global__ void __launch_bounds__(THREADS) attn_kernel(Params p) {
 #pragma unroll
     for (int i = 0; i < RP; ++i) tv[i][0] = tv[i][1] = 0u;
     uint32_t vm = 0;
-#pragma unroll 2
-    for (int u = 0; u < KPT; u += 2) {
-      const int ja = kg + KG * u, jb = kg + KG * (u + 1);
-      const VRaw ra_ = v_raw(vt, ja), rb_ = v_raw(vt, jb);
-      float2 pa[RP], pb[RP];
+    const float* Pk = P + kg * KPT;
 #pragma unroll
-      for (int i = 0; i < RP; ++i) {
-        pa[i] = P2[ja * RP + i];
-        pb[i] = P2[jb * RP + i];
-      }
-      if constexpr (sizeof(KVT) == 2) {
-        absmax_word<KVT>(vm, ra_);
-        absmax_word<KVT>(vm, rb_);
-      } else {
-        absmax_word<KVT>(vm, ra_.x);
-        absmax_word<KVT>(vm, ra_.y);
-        absmax_word<KVT>(vm, rb_.x);
-        absmax_word<KVT>(vm, rb_.y);
-      }
-      const float2 va = v_f32(ra_), vb = v_f32(rb_);
+    for (int u = 0; u < KPT; u += 4) {
+      // p of keys u..u+3 of this thread for every row: one 16-byte load per row
+      float4 pr[RP];
 #pragma unroll
-      for (int i = 0; i < RP; ++i) {
-        const float2 ra = fma2(mul2(pa[i], va), ONE2, C2);
-        const float2 rb = fma2(mul2(pb[i], vb), ONE2, C2);
-        tv[i][0] += __float_as_uint(ra.x) + __float_as_uint(rb.x);
-        tv[i][1] += __float_as_uint(ra.y) + __float_as_uint(rb.y);
+      for (int i = 0; i < RP; ++i) pr[i] = *reinterpret_cast<const float4*>(Pk + i * KT + u);
+#pragma unroll
+      for (int h2 = 0; h2 < 4; h2 += 2) {
+        const int ja = kg + KG * (u + h2), jb = kg + KG * (u + h2 + 1);
+        const VRaw ra_ = v_raw(vt, ja), rb_ = v_raw(vt, jb);
+        if constexpr (sizeof(KVT) == 2) {
+          absmax_word<KVT>(vm, ra_);
+          absmax_word<KVT>(vm, rb_);
+        } else {
+          absmax_word<KVT>(vm, ra_.x);
+          absmax_word<KVT>(vm, ra_.y);
+          absmax_word<KVT>(vm, rb_.x);
+          absmax_word<KVT>(vm, rb_.y);
+        }
+        const float2 va = v_f32(ra_), vb = v_f32(rb_);
+        // (key a, key b) pairs at dim 0 and at dim 1
+        const float2 v0 = make_float2(va.x, vb.x), v1 = make_float2(va.y, vb.y);
+#pragma unroll
+        for (int i = 0; i < RP; ++i) {
+          const float2 pp = h2 == 0 ? make_float2(pr[i].x, pr[i].y) : make_float2(pr[i].z, pr[i].w);
+          const float2 r0 = fma2(mul2(pp, v0), ONE2, C2);
+          const float2 r1 = fma2(mul2(pp, v1), ONE2, C2);
+          tv[i][0] += __float_as_uint(r0.x) + __float_as_uint(r0.y);
+          tv[i][1] += __float_as_uint(r1.x) + __float_as_uint(r1.y);
+        }
       }
     }
     if (absmax_value<KVT>(vm) < vthr) {
@@ -566,7 +571,7 @@ __global__ void __launch_bounds__(THREADS) attn_kernel(Params p) {
 #pragma unroll
         for (int i = 0; i < RP; ++i) {
           if (j >= row_kend[i]) continue;
-          const float ps = P2[jl * RP + i].x;
+          const float ps = P[i * KT + kg * KPT + u];
           const auto x0 = f2x_scaled<BITS>(__fmul_rn(ps, vv.x));
           const auto x1 = f2x_scaled<BITS>(__fmul_rn(ps, vv.y));
           if constexpr (BITS == 64) {
@@ -634,7 +639,7 @@ static int launch(const Params& base, int max_keys, int splits, int req, int ys,
   // score capacity: one split's keys when they fit the budget; keys beyond
   // the capacity are rescored in pass 2
   const int need = ((max_keys + splits - 1) / splits + 15) / 16 * 16 + 16;
-  int cap_max = (int)((kSmemBudget - SM::off_s) / (RP * 4)) / KT * KT;
+  int cap_max = (int)((kSmemBudget - SM::off_s) / (RP * 4) - 8) / KT * KT;
   int cap = (need + KT - 1) / KT * KT;
   if (cap > cap_max) cap = cap_max;
   p.cap = cap;

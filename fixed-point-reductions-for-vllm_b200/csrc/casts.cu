@@ -95,7 +95,18 @@ __global__ void __launch_bounds__(256) fxp_sum_kernel(const T* __restrict__ x, i
     struct alignas(16) V { T v[VEC]; };
     const V* xv = reinterpret_cast<const V*>(xr);
     const int64_t nv = cols / VEC;
-    for (int64_t i = threadIdx.x; i < nv; i += blockDim.x) {
+    int64_t i = threadIdx.x;
+    // four 16-byte loads in flight per thread before any is consumed
+    for (; i + 3 * (int64_t)blockDim.x < nv; i += 4 * (int64_t)blockDim.x) {
+      V t[4];
+#pragma unroll
+      for (int k = 0; k < 4; ++k) t[k] = xv[i + k * blockDim.x];
+#pragma unroll
+      for (int k = 0; k < 4; ++k)
+#pragma unroll
+        for (int e = 0; e < VEC; ++e) acc += f2x_any<BITS>(t[k].v, dtype, e, frac);
+    }
+    for (; i < nv; i += blockDim.x) {
       const V t = xv[i];
 #pragma unroll
       for (int e = 0; e < VEC; ++e) acc += f2x_any<BITS>(t.v, dtype, e, frac);
@@ -130,7 +141,12 @@ template <int BITS>
 static int launch_fxp_sum(const void* x, int dtype, int64_t rows, int64_t cols, int64_t stride,
                           float* out, int frac, cudaStream_t st) {
   const bool aligned = ((uintptr_t)x % 16 == 0) && ((stride * elem_size(dtype)) % 16 == 0);
-  const dim3 grid((unsigned)rows), block(256);
+  // about four 16-byte loads per thread: short rows get small CTAs, so that
+  // many rows are resident per SM
+  const int64_t nvec = cols * elem_size(dtype) / 16;
+  int threads = (int)(((nvec + 4 * 32 - 1) / (4 * 32)) * 32);
+  threads = threads < 64 ? 64 : (threads > 256 ? 256 : threads);
+  const dim3 grid((unsigned)rows), block(threads);
   switch (dtype) {
     case FXPR_BF16:
       if (aligned)

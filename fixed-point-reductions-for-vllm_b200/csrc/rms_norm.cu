@@ -6,6 +6,11 @@
 
 namespace fxpr {
 
+template <typename T> constexpr int x_dtype_of() {
+  return std::is_same<T, __nv_bfloat16>::value ? FXPR_BF16
+         : (std::is_same<T, __half>::value ? FXPR_F16 : FXPR_F32);
+}
+
 template <int BITS, typename XT, int VEC>
 __global__ void __launch_bounds__(256) rms_norm_kernel(
     const XT* __restrict__ x, int64_t xs, const void* __restrict__ w, int w_dtype,
@@ -73,6 +78,95 @@ __global__ void __launch_bounds__(256) rms_norm_kernel(
   }
 }
 
+// Register-resident variant for aligned rows of up to THREADS * MAXV * VEC
+// elements: every 16-byte load of x (and of the residual) is issued before
+// any is consumed, so a CTA keeps the whole row in flight; no shared-memory
+// staging of the row.
+template <int BITS, typename XT, int MAXV, bool RES>
+__global__ void __launch_bounds__(256) rms_norm_vec_kernel(
+    const XT* __restrict__ x, int64_t xs, const void* __restrict__ w, int w_dtype,
+    void* __restrict__ y, int y_dtype, int64_t ys, XT* __restrict__ res, int64_t rs,
+    int64_t hidden, float eps, int frac) {
+  constexpr int VEC = 16 / sizeof(XT);
+  using UAcc = typename std::conditional<BITS == 64, unsigned long long, uint32_t>::type;
+  struct alignas(16) V { XT v[VEC]; };
+  const int64_t row = blockIdx.x;
+  const int nv = (int)(hidden / VEC);
+  const V* xr = reinterpret_cast<const V*>(x + row * xs);
+  V* rr = RES ? reinterpret_cast<V*>(res + row * rs) : nullptr;
+  const float scale = ldexpf(1.0f, frac);
+  V xv[MAXV], rv[MAXV];
+#pragma unroll
+  for (int k = 0; k < MAXV; ++k) {
+    const int j = threadIdx.x + k * blockDim.x;
+    if (j < nv) {
+      xv[k] = xr[j];
+      if (RES) rv[k] = rr[j];
+    }
+  }
+  float xf[MAXV][VEC];
+  UAcc acc = 0;
+#pragma unroll
+  for (int k = 0; k < MAXV; ++k) {
+    const int j = threadIdx.x + k * blockDim.x;
+    if (j < nv) {
+#pragma unroll
+      for (int e = 0; e < VEC; ++e) {
+        float v = to_f32(xv[k].v[e]);
+        if (RES) {
+          v = __fadd_rn(v, to_f32(rv[k].v[e]));  // rms_norm.py:43
+          rv[k].v[e] = from_f32<XT>(v);
+        }
+        xf[k][e] = v;
+        acc += (UAcc)f2x_f32<BITS>(__fmul_rn(v, v), scale);  // rms_norm.py:46-51
+      }
+      if (RES) rr[j] = rv[k];  // rms_norm.py:44
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+  __shared__ UAcc red[8];
+  __shared__ float rrms_s;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (lane == 0) red[warp] = acc;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    UAcc tot = 0;
+    for (int k = 0; k < (int)(blockDim.x >> 5); ++k) tot += red[k];
+    float sum_f;
+    if constexpr (BITS == 64) {
+      sum_f = x2f_f32<64>((long long)tot, ldexpf(1.0f, -frac));
+    } else {
+      sum_f = x2f_f32<32>((int32_t)tot, ldexpf(1.0f, -frac));  // int16 squares sum in int32
+    }
+    const float mean = fmaxf(prim_div(sum_f, (float)hidden), 0.0f);  // rms_norm.py:56
+    rrms_s = prim_div(1.0f, prim_sqrt(__fadd_rn(mean, eps)));       // rms_norm.py:57
+  }
+  __syncthreads();
+  const float rrms = rrms_s;
+  const bool wy_vec = (w_dtype == FXPR_BF16 && y_dtype == FXPR_BF16 && std::is_same<XT, __nv_bfloat16>::value);
+#pragma unroll
+  for (int k = 0; k < MAXV; ++k) {
+    const int j = threadIdx.x + k * blockDim.x;
+    if (j < nv) {
+      if (wy_vec) {
+        const V wv = reinterpret_cast<const V*>(w)[j];
+        V out;
+#pragma unroll
+        for (int e = 0; e < VEC; ++e)
+          out.v[e] = from_f32<XT>(__fmul_rn(__fmul_rn(xf[k][e], to_f32(wv.v[e])), rrms));  // rms_norm.py:59
+        reinterpret_cast<V*>(reinterpret_cast<XT*>(y) + row * ys)[j] = out;
+      } else {
+#pragma unroll
+        for (int e = 0; e < VEC; ++e) {
+          const int64_t i = (int64_t)j * VEC + e;
+          store_f32(y, y_dtype, row * ys + i, __fmul_rn(__fmul_rn(xf[k][e], load_f32(w, w_dtype, i)), rrms));
+        }
+      }
+    }
+  }
+}
+
 template <int BITS, typename XT>
 static int launch_rms(const void* x, int64_t xs, const void* w, int w_dtype, void* y, int y_dtype,
                       int64_t ys, void* res, int res_dtype, int64_t rs, int64_t rows, int64_t hidden,
@@ -80,6 +174,22 @@ static int launch_rms(const void* x, int64_t xs, const void* w, int w_dtype, voi
   constexpr int VEC = 16 / sizeof(XT);
   const size_t smem = (size_t)hidden * sizeof(float);
   const bool aligned = ((uintptr_t)x % 16 == 0) && ((xs * (int64_t)sizeof(XT)) % 16 == 0);
+  const bool res_ok = !res || (res_dtype == x_dtype_of<XT>() && (uintptr_t)res % 16 == 0 &&
+                               (rs * (int64_t)sizeof(XT)) % 16 == 0);
+  const bool y_ok = (uintptr_t)y % 16 == 0 && (ys * elem_size(y_dtype)) % 16 == 0 &&
+                    (uintptr_t)w % 16 == 0;
+  if (aligned && res_ok && y_ok && hidden % VEC == 0 && hidden <= 256 * 4 * VEC) {
+    // enough threads for four 16-byte loads each (more rows resident per SM)
+    const int nvec = (int)(hidden / VEC);
+    const int threads = ((nvec + 4 * 32 - 1) / (4 * 32)) * 32;
+    if (res)
+      rms_norm_vec_kernel<BITS, XT, 4, true><<<(unsigned)rows, threads, 0, st>>>(
+          (const XT*)x, xs, w, w_dtype, y, y_dtype, ys, (XT*)res, rs, hidden, eps, frac);
+    else
+      rms_norm_vec_kernel<BITS, XT, 4, false><<<(unsigned)rows, threads, 0, st>>>(
+          (const XT*)x, xs, w, w_dtype, y, y_dtype, ys, nullptr, 0, hidden, eps, frac);
+    return check_launch("fxpr_rms_norm_fxp");
+  }
   auto k = aligned ? rms_norm_kernel<BITS, XT, VEC> : rms_norm_kernel<BITS, XT, 1>;
   if (smem > 48 * 1024) {
     if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess) {
