@@ -61,6 +61,9 @@ def _compile(src: str) -> tuple[str, bool]:
     obj = os.path.join(BUILD, f"{base}.{_digest(src)}.o")
     if os.path.exists(obj):
         return obj, False
+    for f in os.listdir(BUILD):  # drop stale objects of this source
+        if f.startswith(base + ".") and f.endswith(".o"):
+            os.remove(os.path.join(BUILD, f))
     cmd = [_nvcc(), *NVCC_FLAGS, "-I", INCLUDE, "-c", src, "-o", obj + ".tmp"]
     r = subprocess.run(cmd, capture_output=True, text=True)
     if r.returncode != 0:
