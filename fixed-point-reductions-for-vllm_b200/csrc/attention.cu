@@ -30,7 +30,10 @@ namespace attn {
 
 constexpr int THREADS = 256;
 constexpr int KT = 64;    // keys per tile
-constexpr int NBUF = 3;   // K/V tile buffers (two tiles in flight)
+#ifndef FXPR_ATTN_NBUF
+#define FXPR_ATTN_NBUF 3
+#endif
+constexpr int NBUF = FXPR_ATTN_NBUF;  // K/V tile buffers (NBUF - 1 tiles in flight)
 constexpr int MAX_SPLITS = 8;
 
 struct Params {
@@ -122,7 +125,8 @@ struct Smem {
   static constexpr size_t off_den = off_acc + (size_t)RP * D * 8;
   static constexpr size_t off_stmp = off_den + (size_t)RP * 8;
   static constexpr size_t off_s = off_stmp + (size_t)RP * KT * 4;
-  static size_t bytes(int cap) { return off_s + (size_t)RP * (cap + 8) * 4; }
+  // scores [RP][cap + 8] floats, then the block indices of the first cap keys
+  static size_t bytes(int cap) { return off_s + (size_t)RP * (cap + 8) * 4 + (size_t)cap * 4; }
 };
 
 }  // namespace attn
@@ -174,6 +178,7 @@ __global__ void __launch_bounds__(THREADS) attn_kernel(Params p) {
   unsigned long long* den_s = reinterpret_cast<unsigned long long*>(smem + SM::off_den);
   float* S_tmp = reinterpret_cast<float*>(smem + SM::off_stmp);
   float* S = reinterpret_cast<float*>(smem + SM::off_s);
+  int* blk_cache = reinterpret_cast<int*>(S + RP * (p.cap + 8));  // [cap] physical blocks
 
   __shared__ int row_tok[RP], row_head[RP], row_pos[RP], row_kend[RP];
   __shared__ uint32_t q_or;
@@ -253,31 +258,41 @@ __global__ void __launch_bounds__(THREADS) attn_kernel(Params p) {
   const float vthr = __double2float_rd(fmin(65504.5, 4194304.0 / (scale_d * (1.0 + 1.0 / 1024))));
 
   // ---- tile copies: each thread copies CPT consecutive 16-byte chunks of
-  // one key row (one block-table lookup), XOR-swizzled in shared memory ----
-  auto issue = [&](const void* base, int64_t sb, int64_t ss, int64_t sh, int ti, int b) {
-    const int jl = t / TPK, c0 = (t % TPK) * CPT;
-    const int j = kb + ti * KT + jl;
-    unsigned char* dst = kvbuf + b * TILEB + jl * ROWB;
+  // one key row, XOR-swizzled in shared memory. The physical block of the
+  // row comes from `blk` (looked up ahead of time, see below) ----
+  const int my_jl = t / TPK;
+  auto block_of = [&](int ti) -> int {  // physical block of this thread's key in tile ti
+    const int j = kb + ti * KT + my_jl;
+    if (j >= ke) return -1;
+    const int bi = p.page_shift >= 0 ? (j >> p.page_shift) : j / p.page;
+    return p.bt[bt_row + bi];
+  };
+  auto issue = [&](const void* base, int64_t sb, int64_t ss, int64_t sh, int ti, int b, int blk) {
+    const int c0 = (t % TPK) * CPT;
+    const int j = kb + ti * KT + my_jl;
+    unsigned char* dst = kvbuf + b * TILEB + my_jl * ROWB;
     const unsigned char* src = reinterpret_cast<const unsigned char*>(base);
     int bytes = 0;
-    if (j < ke) {
-      int bi, slot;
-      if (p.page_shift >= 0) {
-        bi = j >> p.page_shift;
-        slot = j & (p.page - 1);
-      } else {
-        bi = j / p.page;
-        slot = j - bi * p.page;
-      }
-      const int64_t blk = p.bt[bt_row + bi];
-      src += (blk * sb + (int64_t)slot * ss + (int64_t)kvh * sh) * (int64_t)sizeof(KVT);
+    if (blk >= 0) {
+      const int slot = p.page_shift >= 0 ? (j & (p.page - 1)) : j % p.page;
+      src += ((int64_t)blk * sb + (int64_t)slot * ss + (int64_t)kvh * sh) * (int64_t)sizeof(KVT);
       bytes = 16;
     }
 #pragma unroll
     for (int u = 0; u < CPT; ++u) {
       const int c = c0 + u;
-      cp_async16(dst + ((c ^ (jl & SWZ)) * 16), src + c * 16, bytes);
+#if FXPR_ATTN_L2PF
+      cp_async16_l2pf(dst + ((c ^ (my_jl & SWZ)) * 16), src + c * 16, bytes);
+#else
+      cp_async16(dst + ((c ^ (my_jl & SWZ)) * 16), src + c * 16, bytes);
+#endif
     }
+  };
+  // block of tile ti: from the shared-memory cache filled in pass 1 when the
+  // tile lies within the score capacity, else from the block table
+  auto cached_block = [&](int ti) -> int {
+    if ((ti + 1) * KT <= p.cap) return blk_cache[ti * KT + my_jl];
+    return block_of(ti);
   };
 
   // ---- scores of one K tile (attention.py:80-148) ----
@@ -402,15 +417,30 @@ __global__ void __launch_bounds__(THREADS) attn_kernel(Params p) {
   };
 
   // ================= pass 1: scores and row max =================
-  issue(p.k, p.k_sb, p.k_ss, p.k_sh, 0, 0);
-  cp_async_commit();
-  if (1 < ntiles) issue(p.k, p.k_sb, p.k_ss, p.k_sh, 1, 1);
-  cp_async_commit();
+  auto remember = [&](int ti, int blk) {
+    if ((t % TPK) == 0 && (ti + 1) * KT <= p.cap) blk_cache[ti * KT + my_jl] = blk;
+  };
+#pragma unroll
+  for (int s0 = 0; s0 < NBUF - 1; ++s0) {
+    if (s0 < ntiles) {
+      const int blk = block_of(s0);
+      remember(s0, blk);
+      issue(p.k, p.k_sb, p.k_ss, p.k_sh, s0, s0, blk);
+    }
+    cp_async_commit();
+  }
+  // the block-table entry of the next tile to issue is loaded one iteration
+  // early, so no global round trip sits in front of a copy
+  int next_blk = (NBUF - 1 < ntiles) ? block_of(NBUF - 1) : -1;
   for (int ti = 0; ti < ntiles; ++ti) {
     const int b = ti % NBUF;
-    cp_async_wait<1>();
-    __syncthreads();  // tile ti visible to all; buffer (ti+2)%3 free
-    if (ti + 2 < ntiles) issue(p.k, p.k_sb, p.k_ss, p.k_sh, ti + 2, (ti + 2) % NBUF);
+    cp_async_wait<NBUF - 2>();
+    __syncthreads();  // tile ti visible to all; buffer (ti+NBUF-1)%NBUF free
+    if (ti + NBUF - 1 < ntiles) {
+      remember(ti + NBUF - 1, next_blk);
+      issue(p.k, p.k_sb, p.k_ss, p.k_sh, ti + NBUF - 1, (ti + NBUF - 1) % NBUF, next_blk);
+      next_blk = (ti + NBUF < ntiles) ? block_of(ti + NBUF) : -1;
+    }
     cp_async_commit();
     const bool store = (ti + 1) * KT <= p.cap;
     qk_tile(ti, b, store ? S : nullptr, p.cap + 8, ti * KT, true);
@@ -432,10 +462,12 @@ __global__ void __launch_bounds__(THREADS) attn_kernel(Params p) {
     rmax_s[t] = m;
   }
   // start streaming V while the maxima are exchanged
-  issue(p.v, p.v_sb, p.v_ss, p.v_sh, 0, 0);
-  cp_async_commit();
-  if (1 < ntiles) issue(p.v, p.v_sb, p.v_ss, p.v_sh, 1, 1);
-  cp_async_commit();
+  __syncthreads();  // block cache complete
+#pragma unroll
+  for (int s0 = 0; s0 < NBUF - 1; ++s0) {
+    if (s0 < ntiles) issue(p.v, p.v_sb, p.v_ss, p.v_sh, s0, s0, cached_block(s0));
+    cp_async_commit();
+  }
   cluster.sync();
   if (t < RP) {
     float m = -INFINITY;
@@ -478,20 +510,22 @@ __global__ void __launch_bounds__(THREADS) attn_kernel(Params p) {
 
   for (int ti = 0; ti < ntiles; ++ti) {
     const int b = ti % NBUF;
-    cp_async_wait<1>();
-    __syncthreads();  // V tile ti visible; previous P2 consumed; buffer (ti+2)%3 free
+    cp_async_wait<NBUF - 2>();
+    __syncthreads();  // V tile ti visible; previous P consumed; buffer (ti+NBUF-1)%NBUF free
     const bool recompute = (ti + 1) * KT > p.cap;
     if (recompute) {
       // scores beyond the capacity: reload this K tile into the free buffer
-      const int kbuf = (ti + 2) % NBUF;
-      issue(p.k, p.k_sb, p.k_ss, p.k_sh, ti, kbuf);
+      const int kbuf = (ti + NBUF - 1) % NBUF;
+      issue(p.k, p.k_sb, p.k_ss, p.k_sh, ti, kbuf, block_of(ti));
       cp_async_commit();
       cp_async_wait<0>();
       __syncthreads();
       qk_tile(ti, kbuf, S_tmp, KT, 0, false);
       __syncthreads();
     }
-    if (ti + 2 < ntiles) issue(p.v, p.v_sb, p.v_ss, p.v_sh, ti + 2, (ti + 2) % NBUF);
+    if (ti + NBUF - 1 < ntiles)
+      issue(p.v, p.v_sb, p.v_ss, p.v_sh, ti + NBUF - 1, (ti + NBUF - 1) % NBUF,
+            cached_block(ti + NBUF - 1));
     cp_async_commit();
 
     // p = exp2(score - max) (attention.py:237), normaliser (238-243)
@@ -639,7 +673,7 @@ static int launch(const Params& base, int max_keys, int splits, int req, int ys,
   // score capacity: one split's keys when they fit the budget; keys beyond
   // the capacity are rescored in pass 2
   const int need = ((max_keys + splits - 1) / splits + 15) / 16 * 16 + 16;
-  int cap_max = (int)((kSmemBudget - SM::off_s) / (RP * 4) - 8) / KT * KT;
+  int cap_max = (int)((kSmemBudget - SM::off_s) / (RP * 4 + 4) - 8) / KT * KT;
   int cap = (need + KT - 1) / KT * KT;
   if (cap > cap_max) cap = cap_max;
   p.cap = cap;
@@ -780,6 +814,17 @@ extern "C" int fxpr_unified_attention_fxp(const fxpr_attention_params* a, void* 
   const int max_useful = (max_keys + attn::KT - 1) / attn::KT;  // no split shorter than a tile
   if (splits > max_useful) splits = max_useful < 1 ? 1 : max_useful;
   const int ys = a->num_kv_heads * p.head_slices;
+  // The split count only changes the schedule, never the result. Use the
+  // knob as an upper bound: once the (request, head, query tile) work items
+  // alone fill about two waves of resident CTAs, extra splits only add
+  // per-CTA fixed cost (metadata loads, q staging, the cluster combine).
+  {
+    const int64_t items = (int64_t)a->num_requests * ys * p.qtiles;
+    const int64_t resident = (int64_t)num_sms() * 3;
+    int64_t want = (2 * resident + items - 1) / items;
+    if (want < 1) want = 1;
+    if (splits > want) splits = (int)want;
+  }
   const cudaStream_t st = (cudaStream_t)stream;
   const int R = a->num_requests;
   switch (D) {
