@@ -349,10 +349,13 @@ def main():
             v, dt, sample = cpu_sample(cores)
             cpu = {"value": round(v, 4), "unit": "GB/s", "cores": cores, "kind": "port",
                    "sample": sample + f" ({dt:.1f} s)"}
-        traffic = None
+        traffic = None  # DRAM bytes per attention launch from the committed ncu launch list
         try:
-            with open(os.path.join(ROOT, "profiles", "attention_traffic.json")) as f:
-                traffic = json.load(f).get("bytes_per_launch")
+            import re
+
+            with open(os.path.join(ROOT, "profiles", "decode_ops_launch_list.md")) as f:
+                m = re.search(r"traffic_bytes_per_launch attn_kernel: (\d+)", f.read())
+            traffic = int(m.group(1)) if m else None
         except Exception:
             pass
         line = {
