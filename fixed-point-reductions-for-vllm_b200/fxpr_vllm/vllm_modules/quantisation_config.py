@@ -30,7 +30,7 @@ from vllm.model_executor.parameter import ModelWeightParameter
 from .. import library_ops  # noqa: F401  (registers torch.ops.fxpr.*)
 from ..fixed_point_kernels.fixed_point import fixed_tl_dtype, int_bits_of
 from .config import DEFAULT_FRAC_BITS, get_runtime_config
-from .tp_allreduce import integer_all_reduce
+from .tp_allreduce import integer_all_reduce_op  # noqa: F401  (registers fxpr::integer_all_reduce)
 
 logger = logging.getLogger("fxpr_vllm")
 
@@ -121,7 +121,7 @@ class FixedPointLinearMethod(QuantizeMethodBase):
             x2d = x2d.contiguous()
         acc = torch.ops.fxpr.gemm_fxp_int(x2d, w_t, self.config.frac_bits, self.fxp_int_bits)
         if getattr(layer, "fxp_int_reduce", False):
-            acc = integer_all_reduce(acc)
+            acc = torch.ops.fxpr.integer_all_reduce(acc)
             # bias after the reduce on every rank (vLLM passes it to rank 0 only)
             if layer.bias is not None and not layer.skip_bias_add:
                 bias = layer.bias

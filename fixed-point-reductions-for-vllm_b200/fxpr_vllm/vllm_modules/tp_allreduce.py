@@ -39,3 +39,16 @@ def integer_all_reduce(t: torch.Tensor, group=None) -> torch.Tensor:
             return out
     dist.all_reduce(t, op=dist.ReduceOp.SUM, group=tp.device_group)
     return t
+
+
+@torch.library.custom_op("fxpr::integer_all_reduce", mutates_args=(), device_types="cuda")
+def integer_all_reduce_op(t: torch.Tensor) -> torch.Tensor:
+    """Opaque op form of :func:`integer_all_reduce` over the vLLM TP group, so
+    that torch.compile and CUDA-graph capture treat it as one node (vLLM's own
+    all-reduce op may route int tensors into float-only custom kernels)."""
+    return integer_all_reduce(t.clone())
+
+
+@integer_all_reduce_op.register_fake
+def _(t):
+    return torch.empty_like(t)
