@@ -21,95 +21,12 @@
 // clamp-and-convert path of the reference runs for that tile.
 #include <cooperative_groups.h>
 
-#include "fxp_common.cuh"
+#include "attention_common.cuh"
 
 namespace cg = cooperative_groups;
 
 namespace fxpr {
 namespace attn {
-
-constexpr int THREADS = 256;
-constexpr int KT = 64;    // keys per tile
-#ifndef FXPR_ATTN_NBUF
-#define FXPR_ATTN_NBUF 3
-#endif
-constexpr int NBUF = FXPR_ATTN_NBUF;  // K/V tile buffers (NBUF - 1 tiles in flight)
-constexpr int MAX_SPLITS = 8;
-
-struct Params {
-  const void* q;
-  int q_dtype;
-  int64_t q_st, q_sh;
-  const void* k;
-  const void* v;
-  int64_t k_sb, k_ss, k_sh;
-  int64_t v_sb, v_ss, v_sh;
-  void* o;
-  int o_dtype;
-  int64_t o_st, o_sh;
-  const int32_t* qsl;
-  const int32_t* seq_lens;
-  const int32_t* bt;
-  int64_t bt_stride;
-  const float* alibi;
-  int num_heads, num_kv_heads, group, gs, head_slices, qt, page;
-  int causal, window;
-  float scale_log2, softcap_log2;
-  int frac;
-  int exact_qk;  // q and K are 16-bit floats: products are exact in fp32
-  int cap;       // score capacity (keys) per CTA
-  int splits;
-  int qtiles;
-  int page_shift;  // log2(page) when page is a power of two, else -1
-  float one;      // 1.0f, opaque to the compiler (magic add as an FMA)
-};
-
-// 16-byte chunk of KV elements -> fp32 pairs
-template <typename T> struct Chunk;
-template <> struct Chunk<__nv_bfloat16> {
-  static constexpr int E = 8;
-  __device__ static __forceinline__ void unpack(uint4 w, float2 (&out)[4]) {
-    const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
-#pragma unroll
-    for (int i = 0; i < 4; ++i)
-      out[i] = make_float2(__uint_as_float(ws[i] << 16), __uint_as_float(ws[i] & 0xFFFF0000u));
-  }
-};
-template <> struct Chunk<__half> {
-  static constexpr int E = 8;
-  __device__ static __forceinline__ void unpack(uint4 w, float2 (&out)[4]) {
-    const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
-#pragma unroll
-    for (int i = 0; i < 4; ++i) out[i] = __half22float2(*reinterpret_cast<const __half2*>(&ws[i]));
-  }
-};
-template <> struct Chunk<float> {
-  static constexpr int E = 4;
-  __device__ static __forceinline__ void unpack(uint4 w, float2 (&out)[2]) {
-    out[0] = make_float2(__uint_as_float(w.x), __uint_as_float(w.y));
-    out[1] = make_float2(__uint_as_float(w.z), __uint_as_float(w.w));
-  }
-};
-
-template <typename T> __device__ __forceinline__ uint32_t chunk_abs_max(uint4 w) {
-  return max(max(abs_max_as_f32<T>(w.x), abs_max_as_f32<T>(w.y)),
-             max(abs_max_as_f32<T>(w.z), abs_max_as_f32<T>(w.w)));
-}
-
-// two V values -> fp32 after the reference's cast to fp16 (attention.py:245-249)
-template <typename T> __device__ __forceinline__ float2 v_pair_f16(const unsigned char* p);
-template <> __device__ __forceinline__ float2 v_pair_f16<__nv_bfloat16>(const unsigned char* p) {
-  const uint32_t w = *reinterpret_cast<const uint32_t*>(p);
-  const float a = __uint_as_float(w << 16), b = __uint_as_float(w & 0xFFFF0000u);
-  return __half22float2(__floats2half2_rn(a, b));
-}
-template <> __device__ __forceinline__ float2 v_pair_f16<__half>(const unsigned char* p) {
-  return __half22float2(*reinterpret_cast<const __half2*>(p));
-}
-template <> __device__ __forceinline__ float2 v_pair_f16<float>(const unsigned char* p) {
-  const float2 f = *reinterpret_cast<const float2*>(p);
-  return __half22float2(__floats2half2_rn(f.x, f.y));
-}
 
 template <int D, int RP, typename KVT>
 struct Smem {
@@ -134,25 +51,6 @@ struct Smem {
 
 namespace fxpr {
 namespace attn {
-
-// Running max of |x| over raw 16-byte chunks / element pairs, kept as packed
-// 16-bit halves (bf16, fp16: one SIMD max per word) or as an fp32 pattern.
-template <typename T> __device__ __forceinline__ void absmax_word(uint32_t& m, uint32_t w) {
-  if constexpr (sizeof(T) == 2) {
-    m = __vmaxu2(m, w & 0x7FFF7FFFu);
-  } else {
-    m = max(m, w & 0x7FFFFFFFu);
-  }
-}
-// the running max as an fp32 value bounding |x| (inf/NaN stay non-finite)
-template <typename T> __device__ __forceinline__ float absmax_value(uint32_t m) {
-  if constexpr (sizeof(T) == 2) {
-    const uint32_t h = max(m & 0xFFFFu, m >> 16);
-    return __uint_as_float(abs_max_as_f32<T>(h));
-  } else {
-    return __uint_as_float(m);
-  }
-}
 
 template <int D, int RP, int BITS, typename KVT>
 __global__ void __launch_bounds__(THREADS) attn_kernel(Params p) {
@@ -748,7 +646,21 @@ static int pick_rp(const Params& p, int rp, int bits, int kv_dtype, int max_keys
 
 using namespace fxpr;
 
-extern "C" int fxpr_unified_attention_fxp(const fxpr_attention_params* a, void* stream) {
+namespace {
+
+// Shape decisions shared by the launch and the workspace query.
+struct Plan {
+  int G, rp, gs, head_slices, qt, qtiles, ys, max_keys, nchunk_max;
+  int64_t items;
+  // chunked-path workspace layout (bytes); total 0 = path not applicable
+  int64_t off_acc, off_den, off_m, off_s, total;
+};
+
+constexpr int64_t kChunkWsLimit = 1ll << 30;
+
+int64_t align256(int64_t x) { return (x + 255) / 256 * 256; }
+
+int validate(const fxpr_attention_params* a) {
   if (!a) {
     set_error("unified_attention_fxp: null params");
     return FXPR_ERR_INVALID;
@@ -775,6 +687,47 @@ extern "C" int fxpr_unified_attention_fxp(const fxpr_attention_params* a, void* 
     set_error("unified_attention_fxp: bad head counts or page size");
     return FXPR_ERR_INVALID;
   }
+  return FXPR_OK;
+}
+
+Plan plan_of(const fxpr_attention_params* a) {
+  Plan pl = {};
+  pl.G = a->num_heads / a->num_kv_heads;
+  pl.rp = (a->max_query_len == 1 && pl.G <= 4) ? 4 : 16;
+  pl.gs = pl.G < pl.rp ? pl.G : pl.rp;
+  pl.head_slices = (pl.G + pl.gs - 1) / pl.gs;
+  pl.qt = pl.rp / pl.gs;
+  pl.qtiles = (a->max_query_len + pl.qt - 1) / pl.qt;
+  pl.ys = a->num_kv_heads * pl.head_slices;
+  const int max_keys = a->max_seq_len > 0 ? a->max_seq_len : a->block_table_cols * a->page_size;
+  pl.max_keys = max_keys < 1 ? 1 : max_keys;
+  pl.nchunk_max = (pl.max_keys + attn::CHUNK - 1) / attn::CHUNK;
+  pl.items = (int64_t)(a->num_requests > 0 ? a->num_requests : 0) * pl.qtiles * pl.ys;
+  if (!attn::chunked_supported(a->head_dim, pl.rp, a->kv_dtype) || pl.items <= 0 ||
+      (int64_t)a->num_requests * pl.qtiles > 65535 || pl.nchunk_max > 65535)
+    return pl;
+  const int64_t rows = pl.items * pl.rp;
+  pl.off_acc = align256(pl.items * 4);
+  pl.off_den = align256(pl.off_acc + rows * a->head_dim * 8);
+  pl.off_m = align256(pl.off_den + rows * 8);
+  pl.off_s = align256(pl.off_m + rows * pl.nchunk_max * 4);
+  const int64_t total = pl.off_s + rows * pl.nchunk_max * attn::CHUNK * 4;
+  if (total <= kChunkWsLimit) pl.total = total;
+  return pl;
+}
+
+}  // namespace
+
+extern "C" int64_t fxpr_attention_workspace_bytes(const fxpr_attention_params* a) {
+  if (validate(a) != FXPR_OK) return 0;
+  if (a->num_requests <= 0 || a->max_query_len <= 0) return 0;
+  return plan_of(a).total;
+}
+
+extern "C" int fxpr_unified_attention_fxp(const fxpr_attention_params* a, void* stream) {
+  const int rc = validate(a);
+  if (rc != FXPR_OK) return rc;
+  const int D = a->head_dim;
   const int es = elem_size(a->kv_dtype);
   const bool aligned = ((uintptr_t)a->k_cache % 16 == 0) && ((uintptr_t)a->v_cache % 16 == 0) &&
                        ((a->k_stride_blk * es) % 16 == 0) && ((a->k_stride_slot * es) % 16 == 0) &&
@@ -785,9 +738,7 @@ extern "C" int fxpr_unified_attention_fxp(const fxpr_attention_params* a, void* 
     return FXPR_ERR_INVALID;
   }
   if (a->num_requests <= 0 || a->max_query_len <= 0) return FXPR_OK;
-  const int G = a->num_heads / a->num_kv_heads;
-  const int rp = (a->max_query_len == 1 && G <= 4) ? 4 : 16;
-  const int gs = G < rp ? G : rp;
+  const Plan pl = plan_of(a);
   attn::Params p = {};
   p.q = a->q; p.q_dtype = a->q_dtype; p.q_st = a->q_stride_tok; p.q_sh = a->q_stride_head;
   p.k = a->k_cache; p.v = a->v_cache;
@@ -796,24 +747,42 @@ extern "C" int fxpr_unified_attention_fxp(const fxpr_attention_params* a, void* 
   p.o = a->o; p.o_dtype = a->o_dtype; p.o_st = a->o_stride_tok; p.o_sh = a->o_stride_head;
   p.qsl = a->query_start_loc; p.seq_lens = a->seq_lens; p.bt = a->block_table;
   p.bt_stride = a->bt_stride; p.alibi = a->alibi_slopes;
-  p.num_heads = a->num_heads; p.num_kv_heads = a->num_kv_heads; p.group = G; p.gs = gs;
-  p.head_slices = (G + gs - 1) / gs; p.qt = rp / gs; p.page = a->page_size;
+  p.num_heads = a->num_heads; p.num_kv_heads = a->num_kv_heads; p.group = pl.G; p.gs = pl.gs;
+  p.head_slices = pl.head_slices; p.qt = pl.qt; p.page = a->page_size;
   p.causal = a->is_causal; p.window = a->window_size;
   p.scale_log2 = a->scale_log2; p.softcap_log2 = a->logits_soft_cap;
   p.frac = a->frac_bits;
   p.exact_qk = (a->q_dtype != FXPR_F32) && (a->kv_dtype != FXPR_F32);
-  p.qtiles = (a->max_query_len + p.qt - 1) / p.qt;
+  p.qtiles = pl.qtiles;
   p.one = 1.0f;
   p.page_shift = -1;
   for (int sh = 0; sh < 31; ++sh)
     if ((1 << sh) == a->page_size) p.page_shift = sh;
-  int max_keys = a->max_seq_len > 0 ? a->max_seq_len : a->block_table_cols * a->page_size;
-  if (max_keys < 1) max_keys = 1;
+  const cudaStream_t st = (cudaStream_t)stream;
+  const int R = a->num_requests;
+
+  if (a->workspace && pl.total > 0 && a->workspace_bytes >= pl.total) {
+    if ((uintptr_t)a->workspace % 256 != 0) {
+      set_error("unified_attention_fxp: workspace must be 256-byte aligned");
+      return FXPR_ERR_INVALID;
+    }
+    unsigned char* ws = reinterpret_cast<unsigned char*>(a->workspace);
+    p.ws_cnt = reinterpret_cast<uint32_t*>(ws);
+    p.ws_acc = reinterpret_cast<unsigned long long*>(ws + pl.off_acc);
+    p.ws_den = reinterpret_cast<unsigned long long*>(ws + pl.off_den);
+    p.ws_m = reinterpret_cast<float*>(ws + pl.off_m);
+    p.ws_s = reinterpret_cast<float*>(ws + pl.off_s);
+    p.nchunk_max = pl.nchunk_max;
+    return attn::launch_chunked(p, D, pl.rp, a->int_bits, a->kv_dtype, R, pl.ys, st);
+  }
+
+  const int max_keys = pl.max_keys;
+  const int rp = pl.rp;
   int splits = a->num_kv_splits < 1 ? 1 : a->num_kv_splits;
   if (splits > attn::MAX_SPLITS) splits = attn::MAX_SPLITS;
   const int max_useful = (max_keys + attn::KT - 1) / attn::KT;  // no split shorter than a tile
   if (splits > max_useful) splits = max_useful < 1 ? 1 : max_useful;
-  const int ys = a->num_kv_heads * p.head_slices;
+  const int ys = pl.ys;
   // The split count only changes the schedule, never the result. Use the
   // knob as an upper bound: once the (request, head, query tile) work items
   // alone fill about two waves of resident CTAs, extra splits only add
@@ -825,8 +794,6 @@ extern "C" int fxpr_unified_attention_fxp(const fxpr_attention_params* a, void* 
     if (want < 1) want = 1;
     if (splits > want) splits = (int)want;
   }
-  const cudaStream_t st = (cudaStream_t)stream;
-  const int R = a->num_requests;
   switch (D) {
     case 32: return attn::pick_rp<32>(p, rp, a->int_bits, a->kv_dtype, max_keys, splits, R, ys, st);
     case 64: return attn::pick_rp<64>(p, rp, a->int_bits, a->kv_dtype, max_keys, splits, R, ys, st);

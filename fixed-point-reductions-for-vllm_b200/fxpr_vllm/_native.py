@@ -13,7 +13,10 @@ import threading
 
 import torch
 
-_LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "_lib", "libfxpr_b200.so")
+# FXPR_B200_LIB: another build of the same library (e.g. with different tile
+# constants); default is the in-tree build
+_LIB_PATH = os.environ.get("FXPR_B200_LIB") or os.path.join(
+    os.path.dirname(os.path.abspath(__file__)), "_lib", "libfxpr_b200.so")
 
 FXPR_OK = 0
 FXPR_ERR_INVALID = -1
@@ -31,7 +34,7 @@ EXPORTED = (
     "fxpr_abi_version", "fxpr_last_error", "fxpr_float_to_fixed", "fxpr_fixed_to_float",
     "fxpr_fxp_sum", "fxpr_gemm_workspace_bytes", "fxpr_gemm_fxp", "fxpr_fixed_to_float_bias",
     "fxpr_rms_norm_fxp", "fxpr_unified_attention_fxp", "fxpr_log_softmax_fxp", "fxpr_probe_prims",
-    "fxpr_gemm_fxp_noalloc",
+    "fxpr_gemm_fxp_noalloc", "fxpr_attention_workspace_bytes",
 )
 
 _i = ctypes.c_int
@@ -59,6 +62,7 @@ class AttentionParams(ctypes.Structure):
         ("scale_log2", _f), ("logits_soft_cap", _f),
         ("frac_bits", ctypes.c_int32), ("int_bits", ctypes.c_int32),
         ("num_kv_splits", ctypes.c_int32),
+        ("workspace", _p), ("workspace_bytes", _i64),
     ]
 
 
@@ -77,6 +81,7 @@ _SIGS = {
     "fxpr_rms_norm_fxp": (_i, [_p, _i, _i64, _p, _i, _p, _i, _i64, _p, _i, _i64, _i64, _i64,
                                _f, _i, _i, _p]),
     "fxpr_unified_attention_fxp": (_i, [ctypes.POINTER(AttentionParams), _p]),
+    "fxpr_attention_workspace_bytes": (_i64, [ctypes.POINTER(AttentionParams)]),
     "fxpr_log_softmax_fxp": (_i, [_p, _i64, _p, _i64, _i64, _i64, _i, _i, _p]),
     "fxpr_probe_prims": (_i, [_i, _p, _p, _p, _i64, _p]),
 }
@@ -151,16 +156,25 @@ def ptr(t: torch.Tensor | None) -> int | None:
 # GEMM split-K workspace: one zero-filled buffer per (device, stream); the
 # kernel leaves it zero-filled after every call.
 # --------------------------------------------------------------------------
-_ws: dict[tuple[int, int], torch.Tensor] = {}
+_ws: dict[tuple[str, int, int], torch.Tensor] = {}
 
 
-def gemm_workspace(device: torch.device, nbytes: int) -> torch.Tensor | None:
+def _workspace(kind: str, device: torch.device, nbytes: int) -> torch.Tensor | None:
     if nbytes <= 0:
         return None
-    key = (device.index if device.index is not None else torch.cuda.current_device(),
+    key = (kind, device.index if device.index is not None else torch.cuda.current_device(),
            stream_ptr(device))
     buf = _ws.get(key)
     if buf is None or buf.numel() < nbytes:
         buf = torch.zeros(max(nbytes, 1 << 20), dtype=torch.uint8, device=device)
         _ws[key] = buf
     return buf
+
+
+def gemm_workspace(device: torch.device, nbytes: int) -> torch.Tensor | None:
+    return _workspace("gemm", device, nbytes)
+
+
+def attention_workspace(device: torch.device, nbytes: int) -> torch.Tensor | None:
+    """Scratch of the chunked attention path (no state between calls)."""
+    return _workspace("attn", device, nbytes)

@@ -40,10 +40,14 @@ def unified_attention_fxp(
     window_size: int = 0,
     num_kv_splits: int | None = None,
     max_seq_len: int | None = None,
+    use_workspace: bool = True,
 ):
     """Run unified prefill + decode attention on a vLLM-layout paged KV cache,
     writing into ``o``. ``block_n``/``d_chunk`` are accepted for signature
-    compatibility (the reference's tile sizes; they do not change results)."""
+    compatibility (the reference's tile sizes; they do not change results).
+    ``max_seq_len`` must bound every ``seq_lens`` entry when given.
+    ``use_workspace=False`` selects the scratch-free cluster path (same
+    results; the chunked path is faster for decode)."""
     assert q.is_cuda and kv_cache.is_cuda, "unified_attention_fxp requires CUDA tensors"
     assert kv_cache.ndim == 5 and kv_cache.shape[1] == 2, (
         "kv_cache must be (num_blocks, 2, block_size, num_kv_heads, head_dim); "
@@ -97,5 +101,11 @@ def unified_attention_fxp(
     p.frac_bits = frac_bits
     p.int_bits = bits
     p.num_kv_splits = int(num_kv_splits)
-    rc = N.load().fxpr_unified_attention_fxp(ctypes.byref(p), N.stream_ptr(q.device))
+    lib = N.load()
+    if use_workspace:
+        need = lib.fxpr_attention_workspace_bytes(ctypes.byref(p))
+        ws = N.attention_workspace(q.device, need)
+        if ws is not None:
+            p.workspace, p.workspace_bytes = ws.data_ptr(), ws.numel()
+    rc = lib.fxpr_unified_attention_fxp(ctypes.byref(p), N.stream_ptr(q.device))
     N.check(rc, "unified_attention_fxp")

@@ -22,7 +22,7 @@
 extern "C" {
 #endif
 
-#define FXPR_ABI_VERSION 1
+#define FXPR_ABI_VERSION 2
 
 /* error codes */
 #define FXPR_OK 0
@@ -140,9 +140,22 @@ typedef struct fxpr_attention_params {
   float logits_soft_cap;          /* logits_soft_cap * (1/ln2) as fp32; 0 = off */
   int32_t frac_bits, int_bits;    /* int_bits 32 or 64 */
   int32_t num_kv_splits;          /* performance knob; results do not depend on it */
+  void* workspace;                /* optional scratch, 256-byte aligned, any contents;
+                                     NULL = cluster path without scratch */
+  int64_t workspace_bytes;
 } fxpr_attention_params;
 
 int fxpr_unified_attention_fxp(const fxpr_attention_params* p, void* stream);
+
+/* Workspace bytes that enable the chunked two-kernel path for this shape
+ * (fixed chunks of keys, uniform work units; results identical to the
+ * cluster path), or 0 when the shape uses the cluster path. Depends on
+ * num_requests, max_query_len, head counts, head_dim, kv dtype and
+ * max_seq_len (or block_table_cols * page_size). max_seq_len must bound
+ * every seq_lens entry. Calls sharing a workspace must be ordered on one
+ * stream. Same interface as fxpr_unified_attention_fxp (attention.py:398-489);
+ * the reference has no workspace. */
+int64_t fxpr_attention_workspace_bytes(const fxpr_attention_params* p);
 
 /* Row-wise log-softmax with a fixed-point exp-sum (softmax.py:8-97): logits
  * rounded to fp16 before the max and exp, [rows, n] fp32 in/out. */

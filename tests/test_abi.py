@@ -28,7 +28,7 @@ def test_library_exports_every_declared_symbol():
 
 
 def test_abi_version():
-    assert N.load().fxpr_abi_version() == 1
+    assert N.load().fxpr_abi_version() == 2
 
 
 def test_invalid_bits_rejected_before_launch():
@@ -93,3 +93,17 @@ def test_fake_impls_shape():
         assert c.shape == (5, 3) and c.dtype == torch.float32
         ci = torch.ops.fxpr.gemm_fxp_int(a, b, 16, 64)
         assert ci.dtype == torch.int64
+
+
+def test_attention_workspace_query():
+    """The workspace query: 0 for shapes the chunked path does not take."""
+    p = N.AttentionParams()
+    p.num_requests, p.max_query_len, p.num_heads, p.num_kv_heads = 64, 1, 32, 8
+    p.head_dim, p.page_size, p.max_seq_len, p.int_bits = 128, 16, 8192, 32
+    p.q_dtype = p.kv_dtype = p.o_dtype = 1
+    need = N.load().fxpr_attention_workspace_bytes(ctypes.byref(p))
+    assert need >= 64 * 8 * 16 * 4 * 512 * 4  # scores of every (item, chunk, row, key)
+    p.max_seq_len = 1 << 24  # scratch beyond the limit: cluster path
+    assert N.load().fxpr_attention_workspace_bytes(ctypes.byref(p)) == 0
+    p.max_seq_len, p.int_bits = 8192, 16  # invalid: 0
+    assert N.load().fxpr_attention_workspace_bytes(ctypes.byref(p)) == 0

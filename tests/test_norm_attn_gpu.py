@@ -81,11 +81,17 @@ def test_rms_norm_config2_bitexact(prims):
 
 # ----------------------------------------------------------------- attention
 def _run_attn(q, kv, qsl, sl, bt, max_q, **kw):
+    """Both device paths (chunked with workspace, cluster without): identical bits."""
     from fxpr_vllm.fixed_point_kernels import attention as A
 
-    o = torch.zeros(q.shape, dtype=torch.float32, device="cuda")
-    A.unified_attention_fxp(q.cuda(), kv.cuda(), o, qsl.cuda(), sl.cuda(), bt.cuda(), max_q, **kw)
-    return o.cpu()
+    outs = []
+    for ws in (True, False):
+        o = torch.zeros(q.shape, dtype=torch.float32, device="cuda")
+        A.unified_attention_fxp(q.cuda(), kv.cuda(), o, qsl.cuda(), sl.cuda(), bt.cuda(), max_q,
+                                use_workspace=ws, **kw)
+        outs.append(o.cpu())
+    assert bits_equal(outs[0], outs[1]), "chunked and cluster paths differ"
+    return outs[0]
 
 
 def _oracle_attn(q, kv, qsl, sl, bt, max_q, prims, bits=32, **kw):
@@ -152,6 +158,41 @@ def test_attention_long_context_rescore(prims):
     assert bits_equal(got, exp)
     got8 = _run_attn(q, kv, qsl, sl, bt, 1, frac_bits=16, num_kv_splits=8)
     assert bits_equal(got8, exp)
+
+
+@pytest.mark.parametrize("bits", [32, 64])
+def test_attention_chunk_boundaries(prims, bits):
+    """Context lengths around the 512-key work units of the chunked path,
+    ragged batch, decode and short prefill rows; the workspace is filled with
+    garbage between calls (it carries no state)."""
+    from fxpr_vllm import _native as N
+
+    lens = [1, 511, 512, 513, 1023, 1024, 1025, 3000]
+    q, kv, qsl, sl, bt = paged_inputs([1] * len(lens), lens, 8, 2, 128, 16, seed=21)
+    exp = _oracle_attn(q, kv, qsl, sl, bt, 1, prims, bits=bits, frac_bits=16)
+    for _ in range(3):
+        got = _run_attn(q, kv, qsl, sl, bt, 1, fxp_dtype=bits, frac_bits=16)
+        assert bits_equal(got, exp), (got - exp).abs().max()
+        for key, buf in N._ws.items():
+            if key[0] == "attn":
+                buf.random_(0, 256)
+    q, kv, qsl, sl, bt = paged_inputs([5, 1, 17], [1030, 513, 600], 8, 2, 64, 16, seed=22)
+    exp = _oracle_attn(q, kv, qsl, sl, bt, 17, prims, bits=bits, frac_bits=16)
+    got = _run_attn(q, kv, qsl, sl, bt, 17, fxp_dtype=bits, frac_bits=16)
+    assert bits_equal(got, exp), (got - exp).abs().max()
+
+
+def test_attention_decode_large_values_rq(prims):
+    """Decode (4-row) scores kernel: lanes on the exact path next to fast ones,
+    64-bit and 32-bit accumulators, several chunks."""
+    q, kv, qsl, sl, bt = paged_inputs([1] * 3, [700, 90, 1500], 8, 2, 128, 16, seed=23)
+    kv = kv.clone()
+    kv[::7] *= 300  # some pages fail the magic-constant guard
+    q = q * 30
+    for bits in (32, 64):
+        exp = _oracle_attn(q, kv, qsl, sl, bt, 1, prims, bits=bits, frac_bits=16)
+        got = _run_attn(q, kv, qsl, sl, bt, 1, fxp_dtype=bits, frac_bits=16)
+        assert bits_equal(got, exp), (bits, (got - exp).abs().max())
 
 
 def test_attention_kv_permutation_invariance():
