@@ -23,6 +23,16 @@
 namespace fxpr {
 namespace attn {
 
+// tile buffers of the two kernels (NBS - 1, NBP - 1 tiles in flight per CTA)
+#ifndef FXPR_ACH_NBS
+#define FXPR_ACH_NBS 3
+#endif
+#ifndef FXPR_ACH_NBP
+#define FXPR_ACH_NBP 3
+#endif
+constexpr int NBS = FXPR_ACH_NBS;
+constexpr int NBP = FXPR_ACH_NBP;
+
 template <int D, typename KVT>
 struct Tile {
   static constexpr int ROWB = D * (int)sizeof(KVT);  // bytes of one key row
@@ -38,13 +48,13 @@ struct ScoreSmem {
   static constexpr size_t off_q = 0;
   static constexpr size_t off_qraw = off_q + (size_t)RP * D * 4;
   static constexpr size_t off_kv = off_qraw + (size_t)RP * D * 4;
-  static constexpr size_t bytes = off_kv + (size_t)NBUF * Tile<D, KVT>::TILEB;
+  static constexpr size_t bytes = off_kv + (size_t)NBS * Tile<D, KVT>::TILEB;
 };
 template <int D, int RP, typename KVT>
 struct PvSmem {
   static constexpr size_t off_p = 0;  // [RP][CHUNK] scores, then p * 2^f
   static constexpr size_t off_kv = off_p + (size_t)RP * CHUNK * 4;
-  static constexpr size_t bytes = off_kv + (size_t)NBUF * Tile<D, KVT>::TILEB;
+  static constexpr size_t bytes = off_kv + (size_t)NBP * Tile<D, KVT>::TILEB;
 };
 
 // Rows of a unit (attention.py:319-353). Returns the key limit over its rows
@@ -214,12 +224,12 @@ __global__ void __launch_bounds__(THREADS) chunk_scores_kernel(Params p) {
 
   TileCopier<D, KVT> cp(p, req, kb, ke, kvh);
 #pragma unroll
-  for (int s0 = 0; s0 < NBUF - 1; ++s0) {
+  for (int s0 = 0; s0 < NBS - 1; ++s0) {
     if (s0 < ntiles)
       cp.issue(p.k, p.k_sb, p.k_ss, p.k_sh, s0, kvbuf + s0 * TILEB, cp.block_of(s0));
     cp_async_commit();
   }
-  int next_blk = (NBUF - 1 < ntiles) ? cp.block_of(NBUF - 1) : -1;
+  int next_blk = (NBS - 1 < ntiles) ? cp.block_of(NBS - 1) : -1;
   clear_item<RP, D>(p, item, chunk, kr_hi);
   const float kthr = stage_q<RP, D>(p, row_tok, row_head, q_s, q_raw, &q_or, scale);
 
@@ -232,17 +242,17 @@ __global__ void __launch_bounds__(THREADS) chunk_scores_kernel(Params p) {
   const int jl = t >> 2, dq = t & 3;
 
   for (int ti = 0; ti < ntiles; ++ti) {
-    cp_async_wait<NBUF - 2>();
-    __syncthreads();  // tile ti visible to all; buffer (ti+NBUF-1)%NBUF free
-    if (ti + NBUF - 1 < ntiles) {
-      cp.issue(p.k, p.k_sb, p.k_ss, p.k_sh, ti + NBUF - 1,
-               kvbuf + ((ti + NBUF - 1) % NBUF) * TILEB, next_blk);
-      next_blk = (ti + NBUF < ntiles) ? cp.block_of(ti + NBUF) : -1;
+    cp_async_wait<NBS - 2>();
+    __syncthreads();  // tile ti visible to all; buffer (ti+NBS-1)%NBS free
+    if (ti + NBS - 1 < ntiles) {
+      cp.issue(p.k, p.k_sb, p.k_ss, p.k_sh, ti + NBS - 1,
+               kvbuf + ((ti + NBS - 1) % NBS) * TILEB, next_blk);
+      next_blk = (ti + NBS < ntiles) ? cp.block_of(ti + NBS) : -1;
     }
     cp_async_commit();
 
     // ---- integer q.k of this thread's quarter of key jl (attention.py:80-118) ----
-    const unsigned char* kt = kvbuf + (ti % NBUF) * TILEB;
+    const unsigned char* kt = kvbuf + (ti % NBS) * TILEB;
     const int j = kb + ti * KT + jl;
     uint32_t acc[RP];
 #pragma unroll
@@ -403,12 +413,12 @@ __global__ void __launch_bounds__(THREADS, 2) chunk_scores_rq_kernel(Params p) {
 
   TileCopier<D, KVT> cp(p, req, kb, ke, kvh);
 #pragma unroll
-  for (int s0 = 0; s0 < NBUF - 1; ++s0) {
+  for (int s0 = 0; s0 < NBS - 1; ++s0) {
     if (s0 < ntiles)
       cp.issue(p.k, p.k_sb, p.k_ss, p.k_sh, s0, kvbuf + s0 * TILEB, cp.block_of(s0));
     cp_async_commit();
   }
-  int next_blk = (NBUF - 1 < ntiles) ? cp.block_of(NBUF - 1) : -1;
+  int next_blk = (NBS - 1 < ntiles) ? cp.block_of(NBS - 1) : -1;
   clear_item<RP, D>(p, item, chunk, kr_hi);
   const float kthr = stage_q<RP, D>(p, row_tok, row_head, q_s, q_raw, &q_or, scale);
 
@@ -430,16 +440,16 @@ __global__ void __launch_bounds__(THREADS, 2) chunk_scores_rq_kernel(Params p) {
   const int my_m = kq >> 2, my_i = kq & 3;  // (key step, row) scored by this lane
 
   for (int ti = 0; ti < ntiles; ++ti) {
-    cp_async_wait<NBUF - 2>();
-    __syncthreads();  // tile ti visible to all; buffer (ti+NBUF-1)%NBUF free
-    if (ti + NBUF - 1 < ntiles) {
-      cp.issue(p.k, p.k_sb, p.k_ss, p.k_sh, ti + NBUF - 1,
-               kvbuf + ((ti + NBUF - 1) % NBUF) * TILEB, next_blk);
-      next_blk = (ti + NBUF < ntiles) ? cp.block_of(ti + NBUF) : -1;
+    cp_async_wait<NBS - 2>();
+    __syncthreads();  // tile ti visible to all; buffer (ti+NBS-1)%NBS free
+    if (ti + NBS - 1 < ntiles) {
+      cp.issue(p.k, p.k_sb, p.k_ss, p.k_sh, ti + NBS - 1,
+               kvbuf + ((ti + NBS - 1) % NBS) * TILEB, next_blk);
+      next_blk = (ti + NBS < ntiles) ? cp.block_of(ti + NBS) : -1;
     }
     cp_async_commit();
 
-    const unsigned char* kt = kvbuf + (ti % NBUF) * TILEB;
+    const unsigned char* kt = kvbuf + (ti % NBS) * TILEB;
     uint4 w[KM][CQ];
 #pragma unroll
     for (int m = 0; m < KM; ++m) {
@@ -454,25 +464,37 @@ __global__ void __launch_bounds__(THREADS, 2) chunk_scores_rq_kernel(Params p) {
     for (int m = 0; m < KM; ++m)
 #pragma unroll
       for (int i = 0; i < RP; ++i) acc[m][i] = 0u;
+    auto body = [&](auto exact) {
 #pragma unroll
-    for (int m = 0; m < KM; ++m)
+      for (int m = 0; m < KM; ++m)
 #pragma unroll
-      for (int h = 0; h < CQ; ++h) {
-        absmax_word<KVT>(km, w[m][h].x);
-        absmax_word<KVT>(km, w[m][h].y);
-        absmax_word<KVT>(km, w[m][h].z);
-        absmax_word<KVT>(km, w[m][h].w);
-        float2 kp[CE / 2];
-        Chunk<KVT>::unpack(w[m][h], kp);
+        for (int h = 0; h < CQ; ++h) {
+          absmax_word<KVT>(km, w[m][h].x);
+          absmax_word<KVT>(km, w[m][h].y);
+          absmax_word<KVT>(km, w[m][h].z);
+          absmax_word<KVT>(km, w[m][h].w);
+          float2 kp[CE / 2];
+          Chunk<KVT>::unpack(w[m][h], kp);
 #pragma unroll
-        for (int i = 0; i < RP; ++i)
+          for (int i = 0; i < RP; ++i)
 #pragma unroll
-          for (int e = 0; e < CE / 2; ++e) {
-            const float2 r = p.exact_qk ? fma2(qr[i][h * CE / 2 + e], kp[e], C2)
-                                        : fma2(mul2(qr[i][h * CE / 2 + e], kp[e]), ONE2, C2);
-            acc[m][i] += __float_as_uint(r.x) + __float_as_uint(r.y);
-          }
-      }
+            for (int e = 0; e < CE / 2; ++e) {
+              float2 r;
+              if constexpr (decltype(exact)::value) {
+                r = fma2(qr[i][h * CE / 2 + e], kp[e], C2);
+              } else {
+                r = fma2(mul2(qr[i][h * CE / 2 + e], kp[e]), ONE2, C2);
+              }
+              acc[m][i] += __float_as_uint(r.x) + __float_as_uint(r.y);
+            }
+        }
+    };
+#ifndef FXPR_ABL_NOMATH
+    if (p.exact_qk) body(std::true_type{});
+    else body(std::false_type{});
+#else
+    acc[0][0] = w[0][0].x; acc[1][0] = w[1][0].y;
+#endif
     const bool fast = absmax_value<KVT>(km) < kthr;
     // 8 partial dots per lane, value index v = m * 4 + i; the reduce-scatter
     // over the 8 lanes of the key group leaves value kq on lane kq
@@ -561,7 +583,9 @@ __global__ void __launch_bounds__(THREADS, 2) chunk_scores_rq_kernel(Params p) {
     const int j = kb + ti * KT + kl + KSTEP * my_m;
     if (j < ke) {
       const float s = score_of<BITS>(p, val, j, row_kend[my_i], row_pos[my_i], row_head[my_i], inv_scale);
+#ifndef FXPR_ABL_NOSTORE
       sdst[my_i * CHUNK + (j - kb)] = s;
+#endif
       rmax = fmaxf(rmax, s);
     }
   }
@@ -593,7 +617,7 @@ __global__ void __launch_bounds__(THREADS) chunk_pv_kernel(Params p) {
   constexpr int KPT = KT / KG;  // PV keys per thread per tile (contiguous)
   using UAcc = typename std::conditional<BITS == 64, unsigned long long, uint32_t>::type;
   static_assert(KPT % 4 == 0 && KPT >= 4, "PV key quads");
-  static_assert((size_t)RP * D * 8 <= (size_t)NBUF * TILEB, "partials reuse the tile buffers");
+  static_assert((size_t)RP * D * 8 <= (size_t)NBP * TILEB, "partials reuse the tile buffers");
 
   extern __shared__ __align__(16) unsigned char smem[];
   float* P_all = reinterpret_cast<float*>(smem + SM::off_p);  // [RP][CHUNK]: score, then p * 2^f
@@ -630,12 +654,12 @@ __global__ void __launch_bounds__(THREADS) chunk_pv_kernel(Params p) {
   }
   TileCopier<D, KVT> cp(p, req, kb, ke, kvh);
 #pragma unroll
-  for (int s0 = 0; s0 < NBUF - 1; ++s0) {
+  for (int s0 = 0; s0 < NBP - 1; ++s0) {
     if (s0 < ntiles)
       cp.issue(p.v, p.v_sb, p.v_ss, p.v_sh, s0, kvbuf + s0 * TILEB, cp.block_of(s0));
     cp_async_commit();
   }
-  int next_blk = (NBUF - 1 < ntiles) ? cp.block_of(NBUF - 1) : -1;
+  int next_blk = (NBP - 1 < ntiles) ? cp.block_of(NBP - 1) : -1;
 
   if (t < RP) {
     den_s[t] = 0ull;
@@ -644,7 +668,7 @@ __global__ void __launch_bounds__(THREADS) chunk_pv_kernel(Params p) {
     for (int c = 0; c < nch; ++c) m = fmaxf(m, mrow[c * RP]);
     gmax_s[t] = m;  // == the reference's pass-1 max over the whole context
   }
-  cp_async_wait<NBUF - 2>();  // scores and V tile 0
+  cp_async_wait<NBP - 2>();  // scores and V tile 0
   __syncthreads();
 
   // ---- p = exp2(score - max) (attention.py:237), normaliser (238-243) ----
@@ -690,31 +714,33 @@ __global__ void __launch_bounds__(THREADS) chunk_pv_kernel(Params p) {
   auto v_raw = [&](const unsigned char* vt, int jl) -> VRaw {
     return *reinterpret_cast<const VRaw*>(vt + jl * ROWB + ((vchunk ^ (jl & SWZ)) * 16) + vin);
   };
-  auto v_f32 = [&](VRaw r) -> float2 {  // fp32(fp16(v)) as the reference computes it
-    if constexpr (sizeof(KVT) == 2) {
-      if (v_exact16) return make_float2(__uint_as_float(r << 16), __uint_as_float(r & 0xFFFF0000u));
-      return v_pair_f16<KVT>(reinterpret_cast<const unsigned char*>(&r));
+  // fp32(fp16(v)) as the reference computes it; E16: the bf16 -> fp16 step is exact
+  auto v_f32 = [&](VRaw r, auto e16) -> float2 {
+    if constexpr (sizeof(KVT) == 2 && std::is_same<KVT, __nv_bfloat16>::value && decltype(e16)::value) {
+      const uint32_t w = reinterpret_cast<const uint32_t&>(r);
+      return make_float2(__uint_as_float(w << 16), __uint_as_float(w & 0xFFFF0000u));
     } else {
       return v_pair_f16<KVT>(reinterpret_cast<const unsigned char*>(&r));
     }
   };
 
   for (int ti = 0; ti < ntiles; ++ti) {
-    if (ti > 0) cp_async_wait<NBUF - 2>();
-    __syncthreads();  // V tile ti (and, first time, p) visible; buffer (ti+NBUF-1)%NBUF free
-    if (ti + NBUF - 1 < ntiles) {
-      cp.issue(p.v, p.v_sb, p.v_ss, p.v_sh, ti + NBUF - 1,
-               kvbuf + ((ti + NBUF - 1) % NBUF) * TILEB, next_blk);
-      next_blk = (ti + NBUF < ntiles) ? cp.block_of(ti + NBUF) : -1;
+    if (ti > 0) cp_async_wait<NBP - 2>();
+    __syncthreads();  // V tile ti (and, first time, p) visible; buffer (ti+NBP-1)%NBP free
+    if (ti + NBP - 1 < ntiles) {
+      cp.issue(p.v, p.v_sb, p.v_ss, p.v_sh, ti + NBP - 1,
+               kvbuf + ((ti + NBP - 1) % NBP) * TILEB, next_blk);
+      next_blk = (ti + NBP < ntiles) ? cp.block_of(ti + NBP) : -1;
     }
     cp_async_commit();
 
-    const unsigned char* vt = kvbuf + (ti % NBUF) * TILEB;
+    const unsigned char* vt = kvbuf + (ti % NBP) * TILEB;
     const float* Pk = P_all + ti * KT + kg * KPT;  // this thread's keys: kg * KPT + u
     uint32_t tv[RP][2];
 #pragma unroll
     for (int i = 0; i < RP; ++i) tv[i][0] = tv[i][1] = 0u;
     uint32_t vm = 0;
+    auto pv_tile = [&](auto e16) {
 #pragma unroll
     for (int u = 0; u < KPT; u += 4) {
       float4 pr[RP];
@@ -733,7 +759,7 @@ __global__ void __launch_bounds__(THREADS) chunk_pv_kernel(Params p) {
           absmax_word<KVT>(vm, rb_.x);
           absmax_word<KVT>(vm, rb_.y);
         }
-        const float2 va = v_f32(ra_), vb = v_f32(rb_);
+        const float2 va = v_f32(ra_, e16), vb = v_f32(rb_, e16);
         const float2 v0 = make_float2(va.x, vb.x), v1 = make_float2(va.y, vb.y);
 #pragma unroll
         for (int i = 0; i < RP; ++i) {
@@ -745,6 +771,13 @@ __global__ void __launch_bounds__(THREADS) chunk_pv_kernel(Params p) {
         }
       }
     }
+    };
+#ifndef FXPR_ABL_NOMATH
+    if (v_exact16) pv_tile(std::true_type{});
+    else pv_tile(std::false_type{});
+#else
+    tv[0][0] = *reinterpret_cast<const uint32_t*>(vt + t * 4);
+#endif
     if (absmax_value<KVT>(vm) < vthr) {
 #pragma unroll
       for (int i = 0; i < RP; ++i)

@@ -103,9 +103,19 @@ template <> __device__ __forceinline__ float2 v_pair_f16<float>(const unsigned c
 
 // Running max of |x| over raw 16-byte chunks / element pairs, kept as packed
 // 16-bit halves (bf16, fp16: one SIMD max per word) or as an fp32 pattern.
+// (16-bit: NaN-propagating packed max of |x|, so NaN keeps the halves NaN and
+// fails the guard)
 template <typename T> __device__ __forceinline__ void absmax_word(uint32_t& m, uint32_t w) {
-  if constexpr (sizeof(T) == 2) {
-    m = __vmaxu2(m, w & 0x7FFF7FFFu);
+  if constexpr (std::is_same<T, __nv_bfloat16>::value) {
+    __nv_bfloat162 a = *reinterpret_cast<__nv_bfloat162*>(&m);
+    const __nv_bfloat162 b = *reinterpret_cast<const __nv_bfloat162*>(&w);
+    a = __hmax2_nan(a, __habs2(b));
+    m = *reinterpret_cast<uint32_t*>(&a);
+  } else if constexpr (std::is_same<T, __half>::value) {
+    __half2 a = *reinterpret_cast<__half2*>(&m);
+    const __half2 b = *reinterpret_cast<const __half2*>(&w);
+    a = __hmax2_nan(a, __habs2(b));
+    m = *reinterpret_cast<uint32_t*>(&a);
   } else {
     m = max(m, w & 0x7FFFFFFFu);
   }
