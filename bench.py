@@ -354,7 +354,7 @@ def main():
             import re
 
             with open(os.path.join(ROOT, "profiles", "decode_ops_launch_list.md")) as f:
-                m = re.search(r"traffic_bytes_per_launch attn_kernel: (\d+)", f.read())
+                m = re.search(r"traffic_bytes_per_call attention: (\d+)", f.read())
             traffic = int(m.group(1)) if m else None
         except Exception:
             pass
@@ -373,14 +373,15 @@ def main():
                            "rms_norm+sum": round((nb["rms_norm"] + nb["fxp_sum"]) / statistics.median(per["rms_norm+sum"]) / 1e6 / peak, 4),
                            "attention": round(achieved / peak, 4)},
                        "gemm_products_per_s": round(64 * 4096 * 4096 / (statistics.median(per["gemm"]) / 1e3), 1)},
-            "roofline": {"kernel": "attn_kernel (paged decode attention)", "bound": "hbm",
+            "roofline": {"kernel": "paged decode attention (chunk_scores + chunk_pv kernels, "
+                                   "2 launches per call)", "bound": "hbm",
                          "achieved": round(achieved, 2), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "traffic": traffic,
                          "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)"},
             "cpu_baseline": cpu,
             "e2e": {"value": round(e2e_val, 3), "unit": "GB/s", "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h},
-            "gpu_launches": 4 * args.steps,
+            "gpu_launches": 5 * args.steps,  # gemm, rms_norm, fxp_sum, 2 x attention
             "clocks": clk.summary(),
         }
         print(json.dumps(line), flush=True)

@@ -33,22 +33,30 @@ namespace attn {
 constexpr int NBS = FXPR_ACH_NBS;
 constexpr int NBP = FXPR_ACH_NBP;
 
-template <int D, typename KVT>
+// keys per tile of the decode scores kernel (the PV kernel and the general
+// scores kernel use KT)
+#ifndef FXPR_ACH_KT
+#define FXPR_ACH_KT 128
+#endif
+constexpr int KTC = FXPR_ACH_KT;
+static_assert(CHUNK % KTC == 0 && CHUNK % KT == 0, "chunk of whole tiles");
+
+template <int D, typename KVT, int NK = KT>
 struct Tile {
   static constexpr int ROWB = D * (int)sizeof(KVT);  // bytes of one key row
   static constexpr int NC = ROWB / 16;               // 16-byte chunks per key row
   static constexpr int SWZ = (NC < 8 ? NC : 8) - 1;  // chunk swizzle mask
-  static constexpr int TILEB = KT * ROWB;
-  static constexpr int TPK = THREADS / KT;  // threads per key row in the copies
+  static constexpr int TILEB = NK * ROWB;
+  static constexpr int TPK = THREADS / NK;  // threads per key row in the copies
   static constexpr int CPT = NC / TPK;      // 16-byte chunks copied per thread
 };
 
-template <int D, int RP, typename KVT>
+template <int D, int RP, typename KVT, int NK = KT>
 struct ScoreSmem {
   static constexpr size_t off_q = 0;
   static constexpr size_t off_qraw = off_q + (size_t)RP * D * 4;
   static constexpr size_t off_kv = off_qraw + (size_t)RP * D * 4;
-  static constexpr size_t bytes = off_kv + (size_t)NBS * Tile<D, KVT>::TILEB;
+  static constexpr size_t bytes = off_kv + (size_t)NBS * Tile<D, KVT, NK>::TILEB;
 };
 template <int D, int RP, typename KVT>
 struct PvSmem {
@@ -94,9 +102,9 @@ __device__ __forceinline__ int unit_rows(const Params& p, int req, int qtile, in
 
 // Copies of one K or V tile: each thread copies CPT consecutive 16-byte
 // chunks of one key row, XOR-swizzled in shared memory.
-template <int D, typename KVT>
+template <int D, typename KVT, int NK = KT>
 struct TileCopier {
-  using TL = Tile<D, KVT>;
+  using TL = Tile<D, KVT, NK>;
   const Params& p;
   int64_t bt_row;
   int kb, ke, kvh, my_jl, c0;
@@ -106,14 +114,14 @@ struct TileCopier {
     c0 = (threadIdx.x % TL::TPK) * TL::CPT;
   }
   __device__ __forceinline__ int block_of(int ti) const {
-    const int j = kb + ti * KT + my_jl;
+    const int j = kb + ti * NK + my_jl;
     if (j >= ke) return -1;
     const int bi = p.page_shift >= 0 ? (j >> p.page_shift) : j / p.page;
     return p.bt[bt_row + bi];
   }
   __device__ __forceinline__ void issue(const void* base, int64_t sb, int64_t ss, int64_t sh,
                                         int ti, unsigned char* dst_tile, int blk) const {
-    const int j = kb + ti * KT + my_jl;
+    const int j = kb + ti * NK + my_jl;
     unsigned char* dst = dst_tile + my_jl * TL::ROWB;
     const unsigned char* src = reinterpret_cast<const unsigned char*>(base);
     int bytes = 0;
@@ -169,18 +177,20 @@ __device__ __forceinline__ float stage_q(const Params& p, const int* row_tok, co
 }
 
 // fp32 score of (row i, key j) from the integer dot (attention.py:119-148);
-// -inf when masked
-template <int BITS>
+// -inf when masked. PL: no softcap, ALiBi or sliding window (checked by the
+// host), so those steps are compiled out.
+template <int BITS, bool PL>
 __device__ __forceinline__ float score_of(const Params& p, long long di, int j, int kend, int pos,
                                           int head, float inv_scale) {
-  if (j >= kend) return -INFINITY;
   float qk = (BITS == 64) ? __ll2float_rn(di) : __int2float_rn((int)di);
   qk = __fmul_rn(__fmul_rn(qk, inv_scale), p.scale_log2);
-  if (p.softcap_log2 > 0.0f) qk = __fmul_rn(p.softcap_log2, prim_tanh(prim_div(qk, p.softcap_log2)));
-  if (p.alibi) qk = __fadd_rn(qk, __fmul_rn(p.alibi[head], __fsub_rn((float)j, (float)pos)));
-  bool ok = true;
+  bool ok = j < kend;
+  if constexpr (!PL) {
+    if (p.softcap_log2 > 0.0f) qk = __fmul_rn(p.softcap_log2, prim_tanh(prim_div(qk, p.softcap_log2)));
+    if (p.alibi) qk = __fadd_rn(qk, __fmul_rn(p.alibi[head], __fsub_rn((float)j, (float)pos)));
+    if (p.window > 0) ok = ok && (j > pos - p.window);
+  }
   if (p.causal) ok = ok && (pos >= j);
-  if (p.window > 0) ok = ok && (j > pos - p.window);
   return ok ? qk : -INFINITY;
 }
 
@@ -188,7 +198,7 @@ __device__ __forceinline__ float score_of(const Params& p, long long di, int j, 
 // kernel 1 (general shapes): scores and chunk row maxima. Four threads share
 // a key (each a quarter of its dims), q read from shared memory.
 // ---------------------------------------------------------------------------
-template <int D, int RP, int BITS, typename KVT>
+template <int D, int RP, int BITS, typename KVT, bool PL>
 __global__ void __launch_bounds__(THREADS) chunk_scores_kernel(Params p) {
   using TL = Tile<D, KVT>;
   using SM = ScoreSmem<D, RP, KVT>;
@@ -342,7 +352,7 @@ __global__ void __launch_bounds__(THREADS) chunk_scores_kernel(Params p) {
 #pragma unroll
         for (int w = 1; w < 4; ++w)
           if (dq == w) di = dot[4 * u + w];
-        const float s = score_of<BITS>(p, di, j, row_kend[i], row_pos[i], row_head[i], inv_scale);
+        const float s = score_of<BITS, PL>(p, di, j, row_kend[i], row_pos[i], row_head[i], inv_scale);
         sdst[i * CHUNK + (j - kb)] = s;
         rmax[u] = fmaxf(rmax[u], s);
       }
@@ -373,19 +383,21 @@ __global__ void __launch_bounds__(THREADS) chunk_scores_kernel(Params p) {
 // once and q never is; the 8 partial dots of (2 keys x 4 rows) are
 // reduce-scattered over the 8 lanes, one score per lane.
 // ---------------------------------------------------------------------------
-template <int D, int BITS, typename KVT>
+template <int D, int BITS, typename KVT, bool PL>
 __global__ void __launch_bounds__(THREADS, 2) chunk_scores_rq_kernel(Params p) {
   constexpr int RP = 4;
-  using TL = Tile<D, KVT>;
-  using SM = ScoreSmem<D, RP, KVT>;
+  using TL = Tile<D, KVT, KTC>;
+  using SM = ScoreSmem<D, RP, KVT, KTC>;
   constexpr int ROWB = TL::ROWB, NC = TL::NC, SWZ = TL::SWZ, TILEB = TL::TILEB;
   constexpr int CE = Chunk<KVT>::E;
   constexpr int TPQ = 8;                // threads per key
   constexpr int KSTEP = THREADS / TPQ;  // keys per step (32)
-  constexpr int KM = KT / KSTEP;        // keys per thread per tile (2)
+  constexpr int KM = KTC / KSTEP;       // keys per thread per tile
   constexpr int CQ = NC / TPQ;          // 16-byte chunks per thread per key
   constexpr int DPT = CQ * CE;          // dims per thread
-  static_assert(NC % TPQ == 0 && KM * RP == TPQ, "rq mapping");
+  constexpr int NV = KM * RP;           // partial dots per lane
+  constexpr int VPL = NV / TPQ;         // scores per lane after the reduce-scatter
+  static_assert(NC % TPQ == 0 && NV % TPQ == 0 && RP % VPL == 0, "rq mapping");
 
   extern __shared__ __align__(16) unsigned char smem[];
   float* q_s = reinterpret_cast<float*>(smem + SM::off_q);
@@ -405,13 +417,13 @@ __global__ void __launch_bounds__(THREADS, 2) chunk_scores_rq_kernel(Params p) {
   const int kb = chunk * CHUNK;
   if (kr_hi < 0 || (chunk > 0 && kb >= kr_hi)) return;  // uniform over the CTA
   const int ke = min(kb + CHUNK, kr_hi);
-  const int ntiles = (ke - kb + KT - 1) / KT;
+  const int ntiles = (ke - kb + KTC - 1) / KTC;
   const int64_t item = (int64_t)blockIdx.z * gridDim.y + blockIdx.y;
   const int64_t unit = item * p.nchunk_max + chunk;
   const float scale = ldexpf(1.0f, p.frac);
   const float inv_scale = ldexpf(1.0f, -p.frac);
 
-  TileCopier<D, KVT> cp(p, req, kb, ke, kvh);
+  TileCopier<D, KVT, KTC> cp(p, req, kb, ke, kvh);
 #pragma unroll
   for (int s0 = 0; s0 < NBS - 1; ++s0) {
     if (s0 < ntiles)
@@ -434,10 +446,14 @@ __global__ void __launch_bounds__(THREADS, 2) chunk_scores_rq_kernel(Params p) {
             *reinterpret_cast<const float2*>(q_s + i * D + (kq + TPQ * h) * CE + e);
 
   float* sdst = p.ws_s + unit * (RP * CHUNK);
-  float rmax = -INFINITY;  // row kq & 3
+  // after the reduce-scatter lane kq holds partial-dot indices VPL*kq + e,
+  // index = m * RP + i: one key step my_m, rows my_i0 + e
+  const int my_m = (VPL * kq) / RP, my_i0 = (VPL * kq) % RP;
+  float rmax[VPL];
+#pragma unroll
+  for (int e = 0; e < VPL; ++e) rmax[e] = -INFINITY;
   const float2 C2 = make_float2(kMagic, kMagic);
   const float2 ONE2 = make_float2(p.one, p.one);
-  const int my_m = kq >> 2, my_i = kq & 3;  // (key step, row) scored by this lane
 
   for (int ti = 0; ti < ntiles; ++ti) {
     cp_async_wait<NBS - 2>();
@@ -498,14 +514,14 @@ __global__ void __launch_bounds__(THREADS, 2) chunk_scores_rq_kernel(Params p) {
     const bool fast = absmax_value<KVT>(km) < kthr;
     // 8 partial dots per lane, value index v = m * 4 + i; the reduce-scatter
     // over the 8 lanes of the key group leaves value kq on lane kq
-    long long val;
+    long long val[VPL];
     if (BITS == 32 || __all_sync(0xffffffffu, fast)) {
-      uint32_t v[TPQ];
+      uint32_t v[NV];
 #pragma unroll
       for (int m = 0; m < KM; ++m)
 #pragma unroll
         for (int i = 0; i < RP; ++i) v[m * RP + i] = acc[m][i] - (uint32_t)DPT * (uint32_t)kMagicBits;
-      if (!fast) {  // BITS == 32 here: exact path, wrapping 32-bit sums
+      if (!__all_sync(0xffffffffu, fast) && !fast) {  // BITS == 32 here: exact path, wrapping sums
 #pragma unroll
         for (int m = 0; m < KM; ++m) {
           const int jl = kl + KSTEP * m;
@@ -527,7 +543,7 @@ __global__ void __launch_bounds__(THREADS, 2) chunk_scores_rq_kernel(Params p) {
         }
       }
 #pragma unroll
-      for (int s = TPQ / 2, n = TPQ; s >= 1; s >>= 1, n >>= 1) {
+      for (int s = TPQ / 2, n = NV; s >= 1; s >>= 1, n >>= 1) {
         const bool hi = (kq & s) != 0;
 #pragma unroll
         for (int k = 0; k < n / 2; ++k) {
@@ -537,10 +553,11 @@ __global__ void __launch_bounds__(THREADS, 2) chunk_scores_rq_kernel(Params p) {
         }
       }
       // fast-path dots of 64-bit runs stay below 2^31 in magnitude
-      val = (BITS == 64) ? (long long)(int32_t)v[0] : (long long)v[0];
+#pragma unroll
+      for (int e = 0; e < VPL; ++e) val[e] = (BITS == 64) ? (long long)(int32_t)v[e] : (long long)v[e];
     } else {
       // 64-bit accumulators with a lane on the exact path somewhere in the warp
-      long long v[TPQ];
+      long long v[NV];
 #pragma unroll
       for (int m = 0; m < KM; ++m)
 #pragma unroll
@@ -568,7 +585,7 @@ __global__ void __launch_bounds__(THREADS, 2) chunk_scores_rq_kernel(Params p) {
         }
       }
 #pragma unroll
-      for (int s = TPQ / 2, n = TPQ; s >= 1; s >>= 1, n >>= 1) {
+      for (int s = TPQ / 2, n = NV; s >= 1; s >>= 1, n >>= 1) {
         const bool hi = (kq & s) != 0;
 #pragma unroll
         for (int k = 0; k < n / 2; ++k) {
@@ -577,24 +594,31 @@ __global__ void __launch_bounds__(THREADS, 2) chunk_scores_rq_kernel(Params p) {
           v[k] = keep + __shfl_xor_sync(0xffffffffu, send, s);
         }
       }
-      val = v[0];
+#pragma unroll
+      for (int e = 0; e < VPL; ++e) val[e] = v[e];
     }
 
-    const int j = kb + ti * KT + kl + KSTEP * my_m;
+    const int j = kb + ti * KTC + kl + KSTEP * my_m;
     if (j < ke) {
-      const float s = score_of<BITS>(p, val, j, row_kend[my_i], row_pos[my_i], row_head[my_i], inv_scale);
+#pragma unroll
+      for (int e = 0; e < VPL; ++e) {
+        const int i = my_i0 + e;
+        const float s = score_of<BITS, PL>(p, val[e], j, row_kend[i], row_pos[i], row_head[i], inv_scale);
 #ifndef FXPR_ABL_NOSTORE
-      sdst[my_i * CHUNK + (j - kb)] = s;
+        sdst[i * CHUNK + (j - kb)] = s;
 #endif
-      rmax = fmaxf(rmax, s);
+        rmax[e] = fmaxf(rmax[e], s);
+      }
     }
   }
   cp_async_wait<0>();
-  // lanes of the same row differ in bits 2..4
-  rmax = fmaxf(rmax, __shfl_xor_sync(0xffffffffu, rmax, 4));
-  rmax = fmaxf(rmax, __shfl_xor_sync(0xffffffffu, rmax, 8));
-  rmax = fmaxf(rmax, __shfl_xor_sync(0xffffffffu, rmax, 16));
-  if (lane < RP) wmax[warp][lane] = rmax;
+  // lanes holding the same rows differ in the bits from RP / VPL up
+#pragma unroll
+  for (int e = 0; e < VPL; ++e) {
+#pragma unroll
+    for (int o = RP / VPL; o < 32; o <<= 1) rmax[e] = fmaxf(rmax[e], __shfl_xor_sync(0xffffffffu, rmax[e], o));
+    if (lane < RP / VPL) wmax[warp][lane * VPL + e] = rmax[e];
+  }
   __syncthreads();
   if (t < RP) {
     float m = -INFINITY;
@@ -870,7 +894,8 @@ constexpr size_t kChunkSmemMax = 200 * 1024;
 
 template <int D, int RP, typename KVT>
 static bool chunk_fits() {
-  return ScoreSmem<D, RP, KVT>::bytes <= kChunkSmemMax && PvSmem<D, RP, KVT>::bytes <= kChunkSmemMax;
+  return ScoreSmem<D, RP, KVT>::bytes <= kChunkSmemMax && ScoreSmem<D, RP, KVT, KTC>::bytes <= kChunkSmemMax &&
+         PvSmem<D, RP, KVT>::bytes <= kChunkSmemMax;
 }
 
 static int configure(const void* k, size_t smem, bool* done) {
@@ -891,16 +916,19 @@ static int launch_chunked_t(const Params& p, int req, int ys, cudaStream_t st) {
     set_error("unified_attention_fxp: chunked path does not fit shared memory");
     return FXPR_ERR_UNSUPPORTED;
   }
-  const size_t s1 = ScoreSmem<D, RP, KVT>::bytes, s2 = PvSmem<D, RP, KVT>::bytes;
+  constexpr bool rq = RP == 4 && (D == 64 || D == 128);
+  const size_t s1 = rq ? ScoreSmem<D, RP, KVT, KTC>::bytes : ScoreSmem<D, RP, KVT>::bytes;
+  const size_t s2 = PvSmem<D, RP, KVT>::bytes;
+  const bool plain = !(p.softcap_log2 > 0.0f) && p.alibi == nullptr && p.window <= 0;
   void (*k1)(Params);
-  if constexpr (RP == 4 && (D == 64 || D == 128)) {
-    k1 = chunk_scores_rq_kernel<D, BITS, KVT>;  // decode: q in registers
+  if constexpr (rq) {  // decode: q in registers
+    k1 = plain ? chunk_scores_rq_kernel<D, BITS, KVT, true> : chunk_scores_rq_kernel<D, BITS, KVT, false>;
   } else {
-    k1 = chunk_scores_kernel<D, RP, BITS, KVT>;
+    k1 = plain ? chunk_scores_kernel<D, RP, BITS, KVT, true> : chunk_scores_kernel<D, RP, BITS, KVT, false>;
   }
   void (*k2)(Params) = chunk_pv_kernel<D, RP, BITS, KVT>;
-  static bool done1[64] = {false}, done2[64] = {false};
-  int rc = configure((const void*)k1, s1, done1);
+  static bool done1[2][64] = {{false}}, done2[64] = {false};
+  int rc = configure((const void*)k1, s1, done1[plain ? 1 : 0]);
   if (rc != FXPR_OK) return rc;
   rc = configure((const void*)k2, s2, done2);
   if (rc != FXPR_OK) return rc;
