@@ -44,5 +44,6 @@ def test_greedy_streams_identical_and_fixed_point_kernels_used(tmp_path):
     assert a["full"] == a["one"] == a["three"]
     assert all(len(s) == 24 for s in a["full"])
     ks = " ".join(a["kernels"])
-    for k in ("gemm_kernel", "rms_norm_kernel", "attn_kernel"):
+    # GEMM, RMSNorm (row or vector variant) and the chunked attention kernels
+    for k in ("gemm_kernel", "rms_norm", "chunk_scores", "chunk_pv_kernel"):
         assert k in ks, (k, a["kernels"])
