@@ -172,6 +172,13 @@ __device__ __forceinline__ unsigned long long f2_bits(float2 v) {
 __device__ __forceinline__ float2 bits_f2(unsigned long long v) {
   return *reinterpret_cast<float2*>(&v);
 }
+#ifndef FXPR_ASM_F32X2
+// compiler builtins for the packed ops (correctly rounded, never contracted),
+// so register pairs are allocated by the compiler rather than through
+// 64-bit asm operands
+__device__ __forceinline__ float2 fma2(float2 a, float2 b, float2 c) { return __ffma2_rn(a, b, c); }
+__device__ __forceinline__ float2 mul2(float2 a, float2 b) { return __fmul2_rn(a, b); }
+#else
 __device__ __forceinline__ float2 fma2(float2 a, float2 b, float2 c) {
   unsigned long long d;
   asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(f2_bits(a)), "l"(f2_bits(b)), "l"(f2_bits(c)));
@@ -182,6 +189,7 @@ __device__ __forceinline__ float2 mul2(float2 a, float2 b) {
   asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(f2_bits(a)), "l"(f2_bits(b)));
   return bits_f2(d);
 }
+#endif
 __device__ __forceinline__ float2 add2(float2 a, float2 b) {
   unsigned long long d;
   asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(f2_bits(a)), "l"(f2_bits(b)));

@@ -31,6 +31,10 @@ constexpr int TN = 4;
 constexpr int THREADS = 256;
 constexpr int STAGES = 3;
 constexpr int A_LD = BK + 4;  // fp32 row pitch of the staged A tile
+#ifndef FXPR_GEMM_KK_UNROLL
+#define FXPR_GEMM_KK_UNROLL 2
+#endif
+constexpr int KK_UNROLL = FXPR_GEMM_KK_UNROLL;  // unroll of the fast k loop
 
 // B tile staging layouts
 enum { B_NCONTIG = 0, B_KCONTIG = 1, B_GENERIC = 2 };
@@ -306,7 +310,7 @@ __global__ void __launch_bounds__(THREADS, MinBlocks<BITS>::v) gemm_kernel(Param
     if (fast) {
       const float2 C2 = make_float2(kMagic, kMagic);
       const float2 ONE2 = make_float2(p.one, p.one);
-#pragma unroll 2
+#pragma unroll KK_UNROLL
       for (int kk = 0; kk < BK; kk += 4) {
         float2 bp[TN][2];
         b_frag(Bb, kk, bp);
