@@ -1,7 +1,7 @@
 """Benchmark of the FxPR fixed-point reduction hot path on B200.
 
 One *step* is one pass of the decode-time hot path over one synthetic batch,
-the three op-level BASELINE configurations back to back on one stream:
+the three op-level benchmark configurations back to back on one stream:
 
   1. fixed-point GEMM   A[64,4096] x W[4096,4096] bf16, Q15.16, int32      (config 1)
   2. fixed-point RMSNorm x[8192,4096] bf16 (int32) + fixed-point row sum  (config 2)
@@ -53,31 +53,49 @@ def _peaks():
 
 
 # ---------------------------------------------------------------- workload
-def make_inputs(seed_base: int = 0):
-    """CPU tensors of the three configs (seeded as SURVEY 8d: fp32 draws then bf16)."""
-    g0 = torch.Generator().manual_seed(seed_base + 0)
-    A = torch.randn(64, 4096, generator=g0).to(torch.bfloat16)
-    W = (torch.randn(4096, 4096, generator=g0) * 0.02).to(torch.bfloat16)
-    g1 = torch.Generator().manual_seed(seed_base + 1)
-    X = torch.randn(8192, 4096, generator=g1).to(torch.bfloat16)
-    Wn = (1 + 0.1 * torch.randn(4096, generator=g1)).to(torch.bfloat16)
-    g2 = torch.Generator().manual_seed(seed_base + 2)
-    ctx = torch.randint(512, 8193, (64,), generator=g2)
-    pool = 40000
-    perm = torch.randperm(pool, generator=g2).to(torch.int32)
+def gemm_inputs(seed: int = 0):
+    """GEMM config: A[64,4096] N(0,1), W[4096,4096] N(0,0.02), fp32 draws then bf16."""
+    g = torch.Generator().manual_seed(seed)
+    A = torch.randn(64, 4096, generator=g).to(torch.bfloat16)
+    W = (torch.randn(4096, 4096, generator=g) * 0.02).to(torch.bfloat16)
+    return dict(A=A, W=W)
+
+
+def norm_inputs(seed: int = 1):
+    """RMSNorm + sum config: x[8192,4096] N(0,1), w[4096] N(1,0.1)."""
+    g = torch.Generator().manual_seed(seed)
+    X = torch.randn(8192, 4096, generator=g).to(torch.bfloat16)
+    Wn = (1 + 0.1 * torch.randn(4096, generator=g)).to(torch.bfloat16)
+    return dict(X=X, Wn=Wn)
+
+
+def attention_inputs(seed: int = 2, batch: int = 64, heads: int = 32, kv_heads: int = 8,
+                     head_dim: int = 128, pool: int = 40000, ctx_lo: int = 512, ctx_hi: int = 8192):
+    """Paged decode attention config: per-request context U[512, 8192], page 16,
+    block tables a random permutation of a 40k-block pool, q and the cache N(0,1)."""
+    g = torch.Generator().manual_seed(seed)
+    ctx = torch.randint(ctx_lo, ctx_hi + 1, (batch,), generator=g)
+    perm = torch.randperm(pool, generator=g).to(torch.int32)
     nblk = (ctx + 15) // 16
-    bt = torch.zeros(64, 512, dtype=torch.int32)
+    bt = torch.zeros(batch, (ctx_hi + 15) // 16, dtype=torch.int32)
     off = 0
-    for r in range(64):
+    for r in range(batch):
         n = int(nblk[r])
         bt[r, :n] = perm[off:off + n]
         off += n
-    Q = torch.randn(64, 32, 128, generator=g2).to(torch.bfloat16)
-    KV = torch.empty(pool, 2, 16, 8, 128, dtype=torch.bfloat16)
+    Q = torch.randn(batch, heads, head_dim, generator=g).to(torch.bfloat16)
+    KV = torch.empty(pool, 2, 16, kv_heads, head_dim, dtype=torch.bfloat16)
     for i in range(0, pool, 2000):  # chunked draw to bound host memory
-        KV[i:i + 2000] = torch.randn(min(2000, pool - i), 2, 16, 8, 128, generator=g2).to(torch.bfloat16)
-    qsl = torch.arange(65, dtype=torch.int32)
-    return dict(A=A, W=W, X=X, Wn=Wn, Q=Q, KV=KV, bt=bt, seq_lens=ctx.to(torch.int32), qsl=qsl)
+        KV[i:i + 2000] = torch.randn(min(2000, pool - i), 2, 16, kv_heads, head_dim,
+                                     generator=g).to(torch.bfloat16)
+    qsl = torch.arange(batch + 1, dtype=torch.int32)
+    return dict(Q=Q, KV=KV, bt=bt, seq_lens=ctx.to(torch.int32), qsl=qsl)
+
+
+def make_inputs(seed_base: int = 0):
+    """CPU tensors of the three op-level configs (fp32 draws then bf16)."""
+    return {**gemm_inputs(seed_base + 0), **norm_inputs(seed_base + 1),
+            **attention_inputs(seed_base + 2)}
 
 
 def algorithmic_bytes(inp) -> dict:
@@ -109,9 +127,12 @@ class Step:
 
     def rms(self):
         from fxpr_vllm.fixed_point_kernels import rms_norm as R
-        from fxpr_vllm.fixed_point_kernels import fixed_point as F
 
         R.rms_norm_fxp(self.d["X"], self.d["Wn"], 1e-6, FRAC, BITS, out=self.y)
+
+    def fsum(self):
+        from fxpr_vllm.fixed_point_kernels import fixed_point as F
+
         return F.fxp_sum(self.d["X"], FRAC, BITS)
 
     def attn(self):
@@ -121,19 +142,18 @@ class Step:
                                 self.d["bt"], 1, fxp_dtype=BITS, frac_bits=FRAC, num_kv_splits=8,
                                 max_seq_len=self.max_seq)
 
+    OPS = ("gemm", "rms_norm", "fxp_sum", "attention")
+
     def run(self, ev=None):
+        fns = (self.gemm, self.rms, self.fsum, self.attn)
         if ev is None:
-            self.gemm()
-            self.rms()
-            self.attn()
+            for fn in fns:
+                fn()
             return
-        ev[0].record()
-        self.gemm()
-        ev[1].record()
-        self.rms()
-        ev[2].record()
-        self.attn()
-        ev[3].record()
+        for i, fn in enumerate(fns):
+            ev[i].record()
+            fn()
+        ev[len(fns)].record()
 
 
 # ---------------------------------------------------------------- clocks
@@ -220,6 +240,32 @@ def cpu_sample(threads: int):
     return nbytes / dt / 1e9, dt, sample
 
 
+# ---------------------------------------------------------------- ncu traffic
+def _ncu_traffic(path):
+    """DRAM bytes per attention call from an ncu CSV of this workload (sum of
+    dram__bytes_read.sum + dram__bytes_write.sum over the attention kernels,
+    divided by the number of calls), or None when no capture is given."""
+    if not path:
+        return None
+    import csv
+
+    per_kernel = {}
+    with open(path) as f:
+        rows = [r for r in csv.reader(line for line in f if not line.startswith("=="))]
+    hdr = rows[0]
+    ki, mi, vi = hdr.index("Kernel Name"), hdr.index("Metric Name"), hdr.index("Metric Value")
+    for r in rows[1:]:
+        if len(r) <= vi or not r[mi].startswith("dram__bytes_"):
+            continue
+        if "attn" not in r[ki]:
+            continue
+        per_kernel.setdefault(r[ki], []).append(float(r[vi].replace(",", "")))
+    if not per_kernel:
+        return None
+    calls = min(len(v) for v in per_kernel.values()) / 2  # read + write rows per launch
+    return int(sum(sum(v) for v in per_kernel.values()) / max(calls, 1))
+
+
 # ---------------------------------------------------------------- main
 def _dist():
     ws = int(os.environ.get("WORLD_SIZE", "1"))
@@ -266,6 +312,9 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--ncu-traffic", default=None,
+                    help="ncu CSV (dram__bytes_read.sum, dram__bytes_write.sum) of this workload: "
+                         "fills roofline.traffic with the attention kernels' DRAM bytes per call")
     args = ap.parse_args()
     ws, rank, local = _dist()
     if args.impl == "reference":
@@ -280,7 +329,8 @@ def main():
     for _ in range(max(args.warmup, 3)):
         st.run()
     torch.cuda.synchronize()
-    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(args.steps)]
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(len(Step.OPS) + 1)]
+           for _ in range(args.steps)]
     if ws > 1:
         torch.distributed.barrier()
     torch.cuda.synchronize()
@@ -299,11 +349,7 @@ def main():
     if ws > 1:
         torch.distributed.barrier()
     t_ms = start.elapsed_time(end)
-    per = {"gemm": [], "rms_norm+sum": [], "attention": []}
-    for e in evs:
-        per["gemm"].append(e[0].elapsed_time(e[1]))
-        per["rms_norm+sum"].append(e[1].elapsed_time(e[2]))
-        per["attention"].append(e[2].elapsed_time(e[3]))
+    per = {op: [e[i].elapsed_time(e[i + 1]) for e in evs] for i, op in enumerate(Step.OPS)}
     if ws > 1:
         tt = torch.tensor([t_ms], device=dev)
         torch.distributed.all_reduce(tt, op=torch.distributed.ReduceOp.MAX)
@@ -325,7 +371,8 @@ def main():
         for k, v in pinned.items():
             st.d[k].copy_(v, non_blocking=True)
         c = st.gemm()
-        s = st.rms()
+        st.rms()
+        s = st.fsum()
         st.attn()
         outs_host = [c.to("cpu", non_blocking=True), st.y.to("cpu", non_blocking=True),
                      s.to("cpu", non_blocking=True), st.o.to("cpu", non_blocking=True)]
@@ -349,15 +396,7 @@ def main():
             v, dt, sample = cpu_sample(cores)
             cpu = {"value": round(v, 4), "unit": "GB/s", "cores": cores, "kind": "port",
                    "sample": sample + f" ({dt:.1f} s)"}
-        traffic = None  # DRAM bytes per attention launch from the committed ncu launch list
-        try:
-            import re
-
-            with open(os.path.join(ROOT, "profiles", "decode_ops_launch_list.md")) as f:
-                m = re.search(r"traffic_bytes_per_call attention: (\d+)", f.read())
-            traffic = int(m.group(1)) if m else None
-        except Exception:
-            pass
+        traffic = _ncu_traffic(args.ncu_traffic)
         line = {
             "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": ws,
             "steps": args.steps, "warmup": max(args.warmup, 3), "ms_per_step": round(ms_step, 4),
@@ -369,9 +408,8 @@ def main():
                        "algorithmic_bytes": nb,
                        "ms_per_op": {k: round(statistics.median(v), 4) for k, v in per.items()},
                        "hbm_frac_per_op": {
-                           "gemm": round(nb["gemm"] / statistics.median(per["gemm"]) / 1e6 / peak, 4),
-                           "rms_norm+sum": round((nb["rms_norm"] + nb["fxp_sum"]) / statistics.median(per["rms_norm+sum"]) / 1e6 / peak, 4),
-                           "attention": round(achieved / peak, 4)},
+                           op: round(nb[op] / statistics.median(per[op]) / 1e6 / peak, 4)
+                           for op in Step.OPS},
                        "gemm_products_per_s": round(64 * 4096 * 4096 / (statistics.median(per["gemm"]) / 1e3), 1)},
             "roofline": {"kernel": "paged decode attention (chunk_scores + chunk_pv kernels, "
                                    "2 launches per call)", "bound": "hbm",

@@ -505,12 +505,8 @@ __global__ void __launch_bounds__(THREADS, 2) chunk_scores_rq_kernel(Params p) {
             }
         }
     };
-#ifndef FXPR_ABL_NOMATH
     if (p.exact_qk) body(std::true_type{});
     else body(std::false_type{});
-#else
-    acc[0][0] = w[0][0].x; acc[1][0] = w[1][0].y;
-#endif
     const bool fast = absmax_value<KVT>(km) < kthr;
     // 8 partial dots per lane, value index v = m * 4 + i; the reduce-scatter
     // over the 8 lanes of the key group leaves value kq on lane kq
@@ -604,9 +600,7 @@ __global__ void __launch_bounds__(THREADS, 2) chunk_scores_rq_kernel(Params p) {
       for (int e = 0; e < VPL; ++e) {
         const int i = my_i0 + e;
         const float s = score_of<BITS, PL>(p, val[e], j, row_kend[i], row_pos[i], row_head[i], inv_scale);
-#ifndef FXPR_ABL_NOSTORE
         sdst[i * CHUNK + (j - kb)] = s;
-#endif
         rmax[e] = fmaxf(rmax[e], s);
       }
     }
@@ -661,7 +655,9 @@ __global__ void __launch_bounds__(THREADS) chunk_pv_kernel(Params p) {
   const int ke = min(kb + CHUNK, kr_hi);
   const int ntiles = (ke - kb + KT - 1) / KT;
   const int nk = ntiles * KT;
-  const int nch = max(1, (kr_hi + CHUNK - 1) / CHUNK);  // units of this item
+  // units of this item; a context beyond the caller's max_seq_len hint is cut
+  // at the workspace's capacity (nchunk_max units) instead of overrunning it
+  const int nch = min(p.nchunk_max, max(1, (kr_hi + CHUNK - 1) / CHUNK));
   const int64_t item = (int64_t)blockIdx.z * gridDim.y + blockIdx.y;
   const int64_t unit = item * p.nchunk_max + chunk;
   const float scale = ldexpf(1.0f, p.frac);
@@ -796,12 +792,8 @@ __global__ void __launch_bounds__(THREADS) chunk_pv_kernel(Params p) {
       }
     }
     };
-#ifndef FXPR_ABL_NOMATH
     if (v_exact16) pv_tile(std::true_type{});
     else pv_tile(std::false_type{});
-#else
-    tv[0][0] = *reinterpret_cast<const uint32_t*>(vt + t * 4);
-#endif
     if (absmax_value<KVT>(vm) < vthr) {
 #pragma unroll
       for (int i = 0; i < RP; ++i)

@@ -20,6 +20,7 @@
 // integer atomics (exact and order-free) into a self-cleaning workspace; the
 // last CTA of a tile (ticket counter) converts and stores the tile and zeroes
 // the workspace and the counter again.
+#include <atomic>
 #include "fxp_common.cuh"
 
 namespace fxpr {
@@ -605,15 +606,18 @@ namespace gemm {
 constexpr int64_t kNoAllocScratchBytes = 8ll << 20;  // 8 MiB per device
 static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
 
+// Per-device address cache. Host threads may race on the first lookup; each
+// stores the same address, and the atomics make the race benign.
 static void* noalloc_scratch_ptr(int* rc) {
-  static void* ptrs[64] = {nullptr};
+  static std::atomic<void*> ptrs[64];
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) {
     set_error("gemm_fxp_noalloc: no current CUDA device");
     *rc = FXPR_ERR_CUDA;
     return nullptr;
   }
-  if (ptrs[dev] == nullptr) {
+  void* cached = ptrs[dev].load(std::memory_order_acquire);
+  if (cached == nullptr) {
     void* p = nullptr;
     const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
     if (e != cudaSuccess || p == nullptr) {
@@ -621,10 +625,11 @@ static void* noalloc_scratch_ptr(int* rc) {
       *rc = FXPR_ERR_CUDA;
       return nullptr;
     }
-    ptrs[dev] = p;
+    ptrs[dev].store(p, std::memory_order_release);
+    cached = p;
   }
   *rc = FXPR_OK;
-  return ptrs[dev];
+  return cached;
 }
 
 }  // namespace gemm

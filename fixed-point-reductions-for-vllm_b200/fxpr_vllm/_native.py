@@ -153,10 +153,18 @@ def ptr(t: torch.Tensor | None) -> int | None:
 
 
 # --------------------------------------------------------------------------
-# GEMM split-K workspace: one zero-filled buffer per (device, stream); the
-# kernel leaves it zero-filled after every call.
+# Kernel scratch: one buffer per (kind, device, stream). The GEMM's split-K
+# scratch is left zero-filled by every call; the attention scratch carries no
+# state between calls.
+#
+# A buffer is never freed once handed out: a CUDA graph captured on the same
+# stream records its address, and replays keep writing there. When a larger
+# call needs more room, the new buffer replaces the old one for later calls,
+# and the old one moves to ``_retired`` (kept alive for the life of the
+# process). Growth is geometric, so few buffers are ever retired.
 # --------------------------------------------------------------------------
 _ws: dict[tuple[str, int, int], torch.Tensor] = {}
+_retired: list[torch.Tensor] = []
 
 
 def _workspace(kind: str, device: torch.device, nbytes: int) -> torch.Tensor | None:
@@ -166,7 +174,11 @@ def _workspace(kind: str, device: torch.device, nbytes: int) -> torch.Tensor | N
            stream_ptr(device))
     buf = _ws.get(key)
     if buf is None or buf.numel() < nbytes:
-        buf = torch.zeros(max(nbytes, 1 << 20), dtype=torch.uint8, device=device)
+        size = max(nbytes, 1 << 20)
+        if buf is not None:
+            size = max(size, 2 * buf.numel())
+            _retired.append(buf)
+        buf = torch.zeros(size, dtype=torch.uint8, device=device)
         _ws[key] = buf
     return buf
 

@@ -4,7 +4,7 @@ Builds a Llama-architecture checkpoint with seeded N(0, 0.02) weights on
 local disk (no network: no tokenizer, token-id prompts), then runs greedy
 decode with ``quantization="fixed_point_det"`` and
 ``attention_backend="CUSTOM"``. Used by the GPU end-to-end test and as the
-decode tokens/s benchmark (BASELINE configs 4 and 5):
+decode tokens/s benchmark (the ~1B and Llama-3-8B architecture workloads):
 
     python -m fxpr_vllm.e2e --preset llama1b --prompts 32 --prompt-len 512 --gen 256 --tp 1
 """
@@ -18,11 +18,11 @@ import sys
 import time
 
 PRESETS = {
-    # BASELINE config 4: ~1B Llama architecture
+    # ~1B Llama architecture
     "llama1b": dict(hidden_size=2048, num_hidden_layers=16, num_attention_heads=32,
                     num_key_value_heads=8, head_dim=64, intermediate_size=8192,
                     rms_norm_eps=1e-5, rope_theta=500000.0, vocab_size=128256),
-    # BASELINE config 5: Llama-3-8B architecture
+    # Llama-3-8B architecture
     "llama8b": dict(hidden_size=4096, num_hidden_layers=32, num_attention_heads=32,
                     num_key_value_heads=8, head_dim=128, intermediate_size=14336,
                     rms_norm_eps=1e-5, rope_theta=500000.0, vocab_size=128256),

@@ -7,11 +7,24 @@ depend on either.
 from __future__ import annotations
 
 import ctypes
+import os
 
 import torch
 
 from .. import _native as N
 from .fixed_point import RCP_LN2, int_bits_of
+
+
+def _validate_hints() -> bool:
+    return os.environ.get("FXPR_VALIDATE_HINTS", "0") not in ("", "0")
+
+
+def check_max_seq_len_hint(seq_lens: torch.Tensor, max_seq_len: int) -> None:
+    """Raise ``ValueError`` if ``max_seq_len`` is below any entry of ``seq_lens``."""
+    longest = int(seq_lens.max()) if seq_lens.numel() else 0
+    if longest > int(max_seq_len):
+        raise ValueError(f"unified_attention_fxp: max_seq_len={int(max_seq_len)} is below the "
+                         f"longest context in seq_lens ({longest})")
 
 
 def prepare_log2_softmax_scale(head_dim, softmax_scale=None):
@@ -45,7 +58,12 @@ def unified_attention_fxp(
     """Run unified prefill + decode attention on a vLLM-layout paged KV cache,
     writing into ``o``. ``block_n``/``d_chunk`` are accepted for signature
     compatibility (the reference's tile sizes; they do not change results).
-    ``max_seq_len`` must bound every ``seq_lens`` entry when given.
+    ``max_seq_len`` must bound every ``seq_lens`` entry when given: keys
+    beyond it are not read (the kernels cut each context at the workspace
+    sized from the hint rather than overrun it). With ``FXPR_VALIDATE_HINTS=1``
+    in the environment the hint is checked against ``seq_lens`` before the
+    launch (a device-to-host read, so not during stream capture) and a
+    violation raises ``ValueError``.
     ``use_workspace=False`` selects the scratch-free cluster path (same
     results; the chunked path is faster for decode)."""
     assert q.is_cuda and kv_cache.is_cuda, "unified_attention_fxp requires CUDA tensors"
@@ -65,6 +83,8 @@ def unified_attention_fxp(
     num_requests = seq_lens.shape[0]
     if num_requests == 0 or max_query_len <= 0:
         return
+    if max_seq_len and _validate_hints() and not torch.cuda.is_current_stream_capturing():
+        check_max_seq_len_hint(seq_lens, max_seq_len)
     assert key_cache.stride(-1) == 1 and value_cache.stride(-1) == 1 and q.stride(-1) == 1 \
         and o.stride(-1) == 1, "head_dim must be the innermost (contiguous) dimension"
     if num_kv_splits is None:

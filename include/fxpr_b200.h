@@ -85,7 +85,8 @@ int fxpr_gemm_fxp(const void* a, int a_dtype, int64_t sam, int64_t sak, const vo
  * reference. The split-K scratch is a fixed 8 MiB array inside the library,
  * one per device; shapes needing more are rejected with FXPR_ERR_INVALID.
  * The first call on a device looks the array up (make it before any stream
- * capture); calls that overlap on the GPU share the array and race. */
+ * capture); the lookup is safe to race from several host threads. Calls that
+ * overlap on the GPU share the array and race. */
 int fxpr_gemm_fxp_noalloc(const void* a, int a_dtype, int64_t sam, int64_t sak, const void* b,
                           int b_dtype, int64_t sbk, int64_t sbn, void* c, int out_kind,
                           int64_t scm, int64_t scn, int64_t M, int64_t N, int64_t K,

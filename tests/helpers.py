@@ -48,7 +48,7 @@ def bits_equal(a: torch.Tensor, b: torch.Tensor) -> bool:
 
 def paged_inputs(qlens, seqlens, H, KVH, D, page, dtype=torch.bfloat16, seed=0, extra_blocks=3):
     """Random paged-attention inputs (CPU tensors): block table is a random
-    permutation of a block pool, like the BASELINE attention config."""
+    permutation of a block pool, like the decode-attention benchmark."""
     g = torch.Generator().manual_seed(seed)
     R = len(qlens)
     T = sum(qlens)

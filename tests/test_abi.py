@@ -107,3 +107,16 @@ def test_attention_workspace_query():
     assert N.load().fxpr_attention_workspace_bytes(ctypes.byref(p)) == 0
     p.max_seq_len, p.int_bits = 8192, 16  # invalid: 0
     assert N.load().fxpr_attention_workspace_bytes(ctypes.byref(p)) == 0
+
+
+
+def test_attention_max_seq_len_hint_check():
+    """An understated max_seq_len hint is reported instead of silently
+    cutting the context (the check FXPR_VALIDATE_HINTS=1 runs before launch)."""
+    from fxpr_vllm.fixed_point_kernels import attention as A
+
+    sl = torch.tensor([100, 900], dtype=torch.int32)
+    A.check_max_seq_len_hint(sl, 900)
+    A.check_max_seq_len_hint(sl[:0], 1)
+    with pytest.raises(ValueError, match="max_seq_len=512"):
+        A.check_max_seq_len_hint(sl, 512)

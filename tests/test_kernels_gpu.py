@@ -152,7 +152,7 @@ def test_gemm_slow_path_saturation_nan(bits):
 
 
 def test_gemm_decode_config_bitexact():
-    """A[64,4096] N(0,1) x W[4096,4096] N(0,0.02), bf16, Q15.16 int32."""
+    """Full benchmark GEMM shape: A[64,4096] N(0,1) x W[4096,4096] N(0,0.02), bf16, Q15.16 int32."""
     _gemm_case(64, 4096, 4096, torch.bfloat16, 32, "ncontig", seed=0)
 
 
@@ -203,3 +203,44 @@ def test_gemm_workspace_left_clean():
     torch.cuda.synchronize()
     for buf in N._ws.values():
         assert int(buf.count_nonzero()) == 0
+
+
+# ------------------------------------------------- linear layer (GEMM + epilogue)
+@pytest.mark.parametrize("bits", [16, 32, 64])
+@pytest.mark.parametrize("out_dtype", [torch.bfloat16, torch.float16, torch.float32])
+@pytest.mark.parametrize("bias_dtype", [None, torch.bfloat16, torch.float32])
+def test_linear_path_matches_oracle(bits, out_dtype, bias_dtype):
+    """The path every model linear layer takes: fxpr::gemm_fxp_int (raw integer
+    accumulator) then fxpr::fixed_to_float_bias (X2F + fp32 bias + cast),
+    against the oracle's FixedPointLinearMethod.apply
+    (reference vllm_modules/quantisation_config.py:163-187)."""
+    from fxpr_vllm import library_ops  # noqa: F401
+
+    g = torch.Generator().manual_seed(bits)
+    f = 8 if bits == 16 else 16
+    for (T, K, N) in [(1, 4096, 512), (7, 1000, 130), (64, 2048, 384)]:
+        x = torch.randn(T, K, generator=g).to(out_dtype)
+        w = (torch.randn(N, K, generator=g) * 0.02).to(torch.bfloat16)
+        bias = None if bias_dtype is None else torch.randn(N, generator=g).to(bias_dtype)
+        acc = torch.ops.fxpr.gemm_fxp_int(x.cuda().to(torch.bfloat16), w.cuda().t(), f, bits)
+        got = torch.ops.fxpr.fixed_to_float_bias(acc, None if bias is None else bias.cuda(), f, bits,
+                                                 out_dtype).cpu()
+        exp = O.linear_apply(x, w, bias, f, bits)
+        assert got.dtype == out_dtype and bits_equal(got, exp), (T, K, N)
+
+
+def test_linear_method_apply_matches_oracle():
+    """FixedPointLinearMethod.apply itself (3-D activations, bias)."""
+    from types import SimpleNamespace
+
+    from fxpr_vllm.vllm_modules.quantisation_config import FixedPointConfig, FixedPointLinearMethod
+
+    g = torch.Generator().manual_seed(7)
+    x = torch.randn(2, 5, 1024, generator=g).to(torch.bfloat16)
+    w = (torch.randn(256, 1024, generator=g) * 0.02).to(torch.bfloat16)
+    bias = torch.randn(256, generator=g).to(torch.bfloat16)
+    m = FixedPointLinearMethod(FixedPointConfig(16))
+    wd = w.cuda()
+    layer = SimpleNamespace(weight_t=wd.t(), fxp_weight=wd, bias=None, fxp_int_reduce=False)
+    got = m.apply(layer, x.cuda(), bias.cuda()).cpu()
+    assert bits_equal(got, O.linear_apply(x, w, bias, 16, m.fxp_int_bits))

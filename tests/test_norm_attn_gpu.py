@@ -66,7 +66,7 @@ def test_rms_norm_row_permutation():
 
 
 def test_rms_norm_config2_bitexact(prims):
-    """x[8192,4096] bf16 N(0,1), w N(1,0.1), eps 1e-6, int32 and int64."""
+    """Full benchmark RMSNorm shape: x[8192,4096] bf16 N(0,1), w N(1,0.1), eps 1e-6, int32 and int64."""
     from fxpr_vllm.fixed_point_kernels import rms_norm as R
     from fxpr_vllm.fixed_point_kernels import fixed_point as F
 
@@ -232,3 +232,62 @@ def test_log_softmax(prims):
         got = S.log_softmax_fxp(c["x"].cuda(), c["bits"], frac_bits=c["frac"]).cpu()
         assert bits_equal(got, O.log_softmax_fxp(c["x"], c["bits"], c["frac"], prims=prims))
         torch.testing.assert_close(got, c["out"], atol=1e-5, rtol=1e-5)
+
+
+def test_workspace_growth_keeps_captured_graph_valid():
+    """A CUDA graph records the workspace address of the call it captured. A
+    later eager call that needs a larger workspace must not free that buffer:
+    replaying the graph afterwards still gives the captured call's result,
+    and the eager call's own result is unaffected."""
+    from fxpr_vllm.fixed_point_kernels import attention as A
+    from fxpr_vllm.fixed_point_kernels import gemm as G
+
+    q, kv, qsl, sl, bt = paged_inputs([1] * 3, [600, 90, 1100], 8, 2, 128, 16, seed=31)
+    dq, dkv, dqsl, dsl, dbt = (t.cuda() for t in (q, kv, qsl, sl, bt))
+    a = torch.randn(16, 2048, device="cuda").to(torch.bfloat16)
+    b = torch.randn(2048, 256, device="cuda").to(torch.bfloat16)
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        o = torch.zeros(q.shape, dtype=torch.float32, device="cuda")
+        A.unified_attention_fxp(dq, dkv, o, dqsl, dsl, dbt, 1, frac_bits=16)  # warm-up, sizes the buffers
+        c = G.gemm_fxp(a, b, 16, 32)
+        torch.cuda.synchronize()
+        expect_o, expect_c = o.clone(), c.clone()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=s):
+            o.zero_()
+            A.unified_attention_fxp(dq, dkv, o, dqsl, dsl, dbt, 1, frac_bits=16)
+            c2 = G.gemm_fxp(a, b, 16, 32)
+        # eager calls on the same stream that need far larger workspaces
+        q3, kv3, qsl3, sl3, bt3 = paged_inputs([1] * 40, [3000] * 40, 8, 2, 128, 16, seed=32)
+        o3 = torch.zeros(q3.shape, dtype=torch.float32, device="cuda")
+        A.unified_attention_fxp(q3.cuda(), kv3.cuda(), o3, qsl3.cuda(), sl3.cuda(), bt3.cuda(), 1,
+                                frac_bits=16)
+        big = G.gemm_fxp(torch.randn(64, 8192, device="cuda").to(torch.bfloat16),
+                         torch.randn(8192, 1024, device="cuda").to(torch.bfloat16), 16, 32)
+        junk = torch.empty(64 << 20, dtype=torch.uint8, device="cuda").fill_(0xAB)  # reuse freed memory
+        for _ in range(3):
+            graph.replay()
+        torch.cuda.synchronize()
+    assert bits_equal(o, expect_o) and bits_equal(c2, expect_c)
+    del junk, big
+
+
+def test_attention_understated_hint(monkeypatch, prims):
+    """A max_seq_len hint below a context length: with FXPR_VALIDATE_HINTS=1
+    the call raises; without it the kernels stay inside the workspace sized
+    from the hint (no overrun) and the other requests are still exact."""
+    from fxpr_vllm.fixed_point_kernels import attention as A
+
+    q, kv, qsl, sl, bt = paged_inputs([1, 1], [300, 2000], 8, 2, 128, 16, seed=41)
+    o = torch.zeros(q.shape, dtype=torch.float32, device="cuda")
+    args = (q.cuda(), kv.cuda(), o, qsl.cuda(), sl.cuda(), bt.cuda(), 1)
+    monkeypatch.setenv("FXPR_VALIDATE_HINTS", "1")
+    with pytest.raises(ValueError, match="max_seq_len"):
+        A.unified_attention_fxp(*args, frac_bits=16, max_seq_len=1000)
+    monkeypatch.setenv("FXPR_VALIDATE_HINTS", "0")
+    A.unified_attention_fxp(*args, frac_bits=16, max_seq_len=1000)
+    torch.cuda.synchronize()
+    exp = _oracle_attn(q[:1], kv, qsl[:2], sl[:1], bt[:1], 1, prims, frac_bits=16)
+    assert bits_equal(o[:1].cpu(), exp)

@@ -12,8 +12,11 @@ import torch
 
 from fxpr_vllm import _native as N
 from fxpr_vllm.fixed_point_kernels import gemm as G
+from oracle import fxp_oracle as O
 
 pytestmark = pytest.mark.gpu
+
+SCRATCH = 8 << 20  # bytes of the library's fixed scratch array
 
 
 def _noalloc(a, b, frac, bits):
@@ -27,29 +30,32 @@ def _noalloc(a, b, frac, bits):
 
 
 @pytest.mark.parametrize("bits", [32, 64])
-def test_noalloc_matches_workspace_entry_twice(bits):
+def test_noalloc_matches_workspace_entry_and_oracle_twice(bits):
     g = torch.Generator().manual_seed(5)
-    a = torch.randn(64, 4096, generator=g).to(torch.bfloat16).cuda()
-    w = (torch.randn(1024, 4096, generator=g) * 0.02).to(torch.bfloat16).cuda()
+    a = torch.randn(64, 4096, generator=g).to(torch.bfloat16)
+    w = (torch.randn(1024, 4096, generator=g) * 0.02).to(torch.bfloat16)
     assert N.load().fxpr_gemm_workspace_bytes(64, 1024, 4096, bits) > 0  # uses the scratch
-    ref = G.gemm_fxp(a, w.t(), 16, bits)
+    exp = O.gemm_fxp(a, w.t(), 16, bits)
+    ad, wd = a.cuda(), w.cuda()
+    ref = G.gemm_fxp(ad, wd.t(), 16, bits)
     for _ in range(2):  # the second call sees the first call's leftover scratch
-        got = _noalloc(a, w.t(), 16, bits)
+        got = _noalloc(ad, wd.t(), 16, bits)
         torch.cuda.synchronize()
         assert torch.equal(got, ref)
+        assert torch.equal(got.cpu(), exp)
 
 
 def test_noalloc_rejects_shapes_beyond_the_scratch():
-    # 140 output tiles with split-K and int64 partials need ~9.2 MB > 8 MiB
-    M, N, K = 64, 140 * 128, 4096
-    need = N_lib().fxpr_gemm_workspace_bytes(M, N, K, 64)
-    if need <= 8 << 20:
-        pytest.skip("shape does not need more than the fixed scratch on this device")
+    lib = N.load()
+    M, K = 64, 4096
+    # split-K (and so the scratch) is used while the output tiles do not fill
+    # the GPU; find a width whose int64 partials need more than the fixed array
+    widths = [128 * t for t in range(1, 4096)
+              if lib.fxpr_gemm_workspace_bytes(M, 128 * t, K, 64) > SCRATCH]
+    if not widths:
+        pytest.skip("no shape on this GPU needs more split-K scratch than the fixed array")
+    N_ = widths[0]
     a = torch.zeros(M, K, dtype=torch.bfloat16, device="cuda")
-    b = torch.zeros(K, N, dtype=torch.bfloat16, device="cuda")
+    b = torch.zeros(K, N_, dtype=torch.bfloat16, device="cuda")
     with pytest.raises(ValueError, match="scratch"):
         _noalloc(a, b, 16, 64)
-
-
-def N_lib():
-    return N.load()
