@@ -651,6 +651,7 @@ namespace {
 // Shape decisions shared by the launch and the workspace query.
 struct Plan {
   int G, rp, gs, head_slices, qt, qtiles, ys, max_keys, nchunk_max;
+  int decode_kmax;  // > 0: the decode path runs, keys per context capped here
   int64_t items;
   // chunked-path workspace layout (bytes); total 0 = path not applicable
   int64_t off_acc, off_den, off_m, off_s, total;
@@ -703,6 +704,17 @@ Plan plan_of(const fxpr_attention_params* a) {
   pl.max_keys = max_keys < 1 ? 1 : max_keys;
   pl.nchunk_max = (pl.max_keys + attn::CHUNK - 1) / attn::CHUNK;
   pl.items = (int64_t)(a->num_requests > 0 ? a->num_requests : 0) * pl.qtiles * pl.ys;
+  pl.decode_kmax = 0;
+  if (a->num_requests > 0 && attn::decode_supported(a, pl.G)) {
+    const int64_t cap = (int64_t)a->block_table_cols * a->page_size;
+    const int kmax = (int)(pl.max_keys < cap ? pl.max_keys : cap);
+    const int64_t need = attn::decode_workspace_bytes(a->num_requests * a->num_kv_heads, kmax, a->head_dim);
+    if (kmax > 0 && need <= kChunkWsLimit) {
+      pl.decode_kmax = kmax;
+      pl.total = need;
+      return pl;
+    }
+  }
   if (!attn::chunked_supported(a->head_dim, pl.rp, a->kv_dtype) || pl.items <= 0 ||
       (int64_t)a->num_requests * pl.qtiles > 65535 || pl.nchunk_max > 65535)
     return pl;
@@ -766,6 +778,7 @@ extern "C" int fxpr_unified_attention_fxp(const fxpr_attention_params* a, void* 
       set_error("unified_attention_fxp: workspace must be 256-byte aligned");
       return FXPR_ERR_INVALID;
     }
+    if (pl.decode_kmax > 0) return attn::launch_decode(a, pl.decode_kmax, a->workspace, st);
     unsigned char* ws = reinterpret_cast<unsigned char*>(a->workspace);
     p.ws_cnt = reinterpret_cast<uint32_t*>(ws);
     p.ws_acc = reinterpret_cast<unsigned long long*>(ws + pl.off_acc);

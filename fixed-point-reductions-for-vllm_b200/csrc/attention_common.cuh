@@ -130,6 +130,11 @@ template <typename T> __device__ __forceinline__ float absmax_value(uint32_t m) 
   }
 }
 
+// decode path for grouped-query batches (attention_decode.cu)
+bool decode_supported(const fxpr_attention_params* a, int G);
+int64_t decode_workspace_bytes(int items, int kmax, int D);
+int launch_decode(const fxpr_attention_params* a, int kmax, void* workspace, cudaStream_t st);
+
 // chunked two-kernel path (attention_chunked.cu)
 bool chunked_supported(int D, int rp, int kv_dtype);
 int launch_chunked(const Params& p, int D, int rp, int bits, int kv_dtype, int req, int ys,

@@ -2,7 +2,12 @@
 #include <cstdarg>
 #include <cstdio>
 
+#include <atomic>
+
+#include <cudaTypedefs.h>
+
 #include "fxp_common.cuh"
+#include "tma.cuh"
 
 namespace fxpr {
 
@@ -36,6 +41,46 @@ int num_sms() {
   }
   return cache[dev];
 }
+
+namespace tma {
+
+static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static std::atomic<PFN_cuTensorMapEncodeTiled_v12000> fn{nullptr};
+  PFN_cuTensorMapEncodeTiled_v12000 f = fn.load(std::memory_order_acquire);
+  if (f == nullptr) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q = cudaDriverEntryPointSymbolNotFound;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess || p == nullptr)
+      return nullptr;
+    f = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    fn.store(f, std::memory_order_release);
+  }
+  return f;
+}
+
+bool encode_4d_u16(CUtensorMap* map, const void* base, const uint64_t dims[4],
+                   const uint64_t strides_bytes[3], const uint32_t box[4]) {
+  PFN_cuTensorMapEncodeTiled_v12000 f = encode_fn();
+  if (f == nullptr) {
+    set_error("cuTensorMapEncodeTiled is not available from the driver");
+    return false;
+  }
+  const cuuint32_t elem_strides[4] = {1, 1, 1, 1};
+  cuuint64_t gd[4] = {dims[0], dims[1], dims[2], dims[3]};
+  cuuint64_t gs[3] = {strides_bytes[0], strides_bytes[1], strides_bytes[2]};
+  cuuint32_t bx[4] = {box[0], box[1], box[2], box[3]};
+  const CUresult r = f(map, CU_TENSOR_MAP_DATA_TYPE_UINT16, 4, const_cast<void*>(base), gd, gs, bx,
+                       elem_strides, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                       CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    set_error("cuTensorMapEncodeTiled failed (%d)", (int)r);
+    return false;
+  }
+  return true;
+}
+
+}  // namespace tma
 
 }  // namespace fxpr
 

@@ -63,6 +63,7 @@ class AttentionParams(ctypes.Structure):
         ("frac_bits", ctypes.c_int32), ("int_bits", ctypes.c_int32),
         ("num_kv_splits", ctypes.c_int32),
         ("workspace", _p), ("workspace_bytes", _i64),
+        ("num_blocks", _i64),
     ]
 
 

@@ -114,6 +114,7 @@ def unified_attention_fxp(
     p.num_kv_heads = key_cache.shape[2]
     p.head_dim = head_dim
     p.page_size = key_cache.shape[1]
+    p.num_blocks = key_cache.shape[0]
     p.is_causal = 1 if is_causal else 0
     p.window_size = int(window_size)
     p.scale_log2 = prepare_log2_softmax_scale(head_dim_query, softmax_scale)

@@ -22,7 +22,7 @@
 extern "C" {
 #endif
 
-#define FXPR_ABI_VERSION 2
+#define FXPR_ABI_VERSION 3
 
 /* error codes */
 #define FXPR_OK 0
@@ -144,6 +144,9 @@ typedef struct fxpr_attention_params {
   void* workspace;                /* optional scratch, 256-byte aligned, any contents;
                                      NULL = cluster path without scratch */
   int64_t workspace_bytes;
+  int64_t num_blocks;             /* blocks in the paged cache (leading dim), 0 = unknown;
+                                     with it, decode batches take the TMA page path and a
+                                     block id outside [0, num_blocks) reads zeros */
 } fxpr_attention_params;
 
 int fxpr_unified_attention_fxp(const fxpr_attention_params* p, void* stream);

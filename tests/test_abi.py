@@ -28,7 +28,7 @@ def test_library_exports_every_declared_symbol():
 
 
 def test_abi_version():
-    assert N.load().fxpr_abi_version() == 2
+    assert N.load().fxpr_abi_version() == 3
 
 
 def test_invalid_bits_rejected_before_launch():
