@@ -411,7 +411,7 @@ def main():
                            op: round(nb[op] / statistics.median(per[op]) / 1e6 / peak, 4)
                            for op in Step.OPS},
                        "gemm_products_per_s": round(64 * 4096 * 4096 / (statistics.median(per["gemm"]) / 1e3), 1)},
-            "roofline": {"kernel": "paged decode attention (chunk_scores + chunk_pv kernels, "
+            "roofline": {"kernel": "paged decode attention (dq_scores + dq_pv kernels, "
                                    "2 launches per call)", "bound": "hbm",
                          "achieved": round(achieved, 2), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "traffic": traffic,

@@ -31,7 +31,16 @@ namespace fxpr {
 namespace attn {
 namespace dq {
 
-constexpr int W = 4;       // warps (workers) per CTA
+#ifndef FXPR_DQ_WARPS
+#define FXPR_DQ_WARPS 4
+#endif
+#ifndef FXPR_DQ_MINB1
+#define FXPR_DQ_MINB1 4
+#endif
+#ifndef FXPR_DQ_MINB2
+#define FXPR_DQ_MINB2 4
+#endif
+constexpr int W = FXPR_DQ_WARPS;  // warps (workers) per CTA
 constexpr int PG = 16;     // keys per page tile
 constexpr int RP = 4;      // query rows per item (the GQA group)
 constexpr int TPK = 8;     // lanes sharing one key in the scores kernel
@@ -128,31 +137,57 @@ __device__ __forceinline__ void locate(const DqParams& p, const int* pre, int G,
   *np_out = np;
 }
 
-// one lane's view of page (base + lane) of the warp's slice
+// one lane's view of page (base + lane) of the warp's slice: item, page in
+// the item, and the TMA coordinates of its box (cache block; kv head and
+// first slot packed as kvh | slot0 << 16)
 struct Slot {
-  int item, pg, blk;
+  int item, pg, blk, kc;
 };
 
 __device__ __forceinline__ Slot resolve(const DqParams& p, const int* pre, int base, int G1) {
-  Slot s{-1, 0, 0};
+  Slot s{-1, 0, 0, 0};
   const int G = base + (int)(threadIdx.x & 31);
   if (G < G1) {
     int np;
     locate(p, pre, G, &s.item, &s.pg, &np);
     const int r = s.item / p.KVH;
+    const int kvh = s.item - r * p.KVH;
     const int key0 = s.pg * PG;
     const int col = p.page_shift >= 0 ? (key0 >> p.page_shift) : key0 / p.page;
+    const int slot0 = key0 - col * p.page;
+    s.kc = kvh | (slot0 << 16);
     s.blk = __ldg(p.bt + (int64_t)r * p.bt_stride + col);
   }
   return s;
 }
 
-__device__ __forceinline__ Slot slot_of(const Slot& a, const Slot& b, bool use_b, int l) {
-  Slot s;
-  s.item = __shfl_sync(0xffffffffu, use_b ? b.item : a.item, l);
-  s.pg = __shfl_sync(0xffffffffu, use_b ? b.pg : a.pg, l);
-  s.blk = __shfl_sync(0xffffffffu, use_b ? b.blk : a.blk, l);
-  return s;
+// 32-bit shared-memory loads and stores
+__device__ __forceinline__ uint4 lds128(uint32_t a) {
+  uint4 v;
+  asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "r"(a));
+  return v;
+}
+__device__ __forceinline__ float4 lds128f(uint32_t a) {
+  float4 v;
+  asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];"
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+               : "r"(a));
+  return v;
+}
+__device__ __forceinline__ uint2 lds64(uint32_t a) {
+  uint2 v;
+  asm volatile("ld.shared.v2.u32 {%0, %1}, [%2];" : "=r"(v.x), "=r"(v.y) : "r"(a));
+  return v;
+}
+__device__ __forceinline__ uint32_t lds32(uint32_t a) {
+  uint32_t v;
+  asm volatile("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(a));
+  return v;
+}
+__device__ __forceinline__ void sts64f(uint32_t a, float x, float y) {
+  asm volatile("st.shared.v2.f32 [%0], {%1, %2};" ::"r"(a), "f"(x), "f"(y) : "memory");
 }
 
 // Running |x| bound over raw 16-bit element pairs without unpacking: the
@@ -216,17 +251,77 @@ __device__ __forceinline__ void drain(uint64_t* bars, int i, int n) {
   for (int k = i + 1; k < n && k < i + S; ++k) (void)tma::mbar_wait(&bars[k % S], (uint32_t)((k / S) & 1));
 }
 
+// Per-warp page pipeline: the slice's page list in two 32-page batches of
+// lane-held slots (A: current, B: next, resolved 32 pages ahead so their
+// block-table reads land early), and the TMA issue of page i into buffer
+// i % S.
+struct Pipe {
+  Slot A, B;
+  int a_idx;
+  __device__ __forceinline__ void advance(const DqParams& p, const int* pre, int G0, int G1) {
+    A = B;
+    ++a_idx;
+    B = resolve(p, pre, G0 + (a_idx + 1) * 32, G1);
+  }
+  // (item, pg) of page i (in batch A)
+  __device__ __forceinline__ int2 item_pg(int i) const {
+    return make_int2(__shfl_sync(0xffffffffu, A.item, i & 31), __shfl_sync(0xffffffffu, A.pg, i & 31));
+  }
+  // coordinates of page i: (kv head | slot0 << 16, block)
+  __device__ __forceinline__ int2 coords(int i) const {
+    const bool b = (i >> 5) != a_idx;
+    return make_int2(__shfl_sync(0xffffffffu, b ? B.kc : A.kc, i & 31),
+                     __shfl_sync(0xffffffffu, b ? B.blk : A.blk, i & 31));
+  }
+};
+
 // ---------------------------------------------------------------------------
 // kernel 1: scores and page row maxima
 // ---------------------------------------------------------------------------
+// exact q.k partial dots of one lane (keys kA and kA + 4, its dims), every
+// product clamped and rounded on its own; the rare path for values the
+// magic-constant rounding cannot take (large, inf, NaN)
+struct Dots8 {
+  unsigned long long v[8];
+};
 template <int D, int BITS, typename T>
-__global__ void __launch_bounds__(W * 32, 4)
+__device__ __forceinline__ Dots8 exact_dots(const T* qbase, int64_t q_sh, uint32_t kt, int kA, int kq,
+                                         float scale) {
+  using GE = Geo<D>;
+  Dots8 r;
+#pragma unroll
+  for (int v = 0; v < 8; ++v) r.v[v] = 0ull;
+#pragma unroll 1
+  for (int h = 0; h < GE::CQ; ++h) {
+    const int c = kq + TPK * h;
+#pragma unroll 1
+    for (int e = 0; e < 8; ++e) {
+      float qf[RP];
+#pragma unroll
+      for (int row = 0; row < RP; ++row) qf[row] = to_f32(qbase[row * q_sh + c * 8 + e]);
+#pragma unroll
+      for (int mm = 0; mm < 2; ++mm) {
+        const uint32_t w = lds32(kt + (kA + 4 * mm) * GE::ROWB + c * 16 + (e >> 1) * 4);
+        const uint16_t bitsk = (uint16_t)(w >> (16 * (e & 1)));
+        const float kf = to_f32(*reinterpret_cast<const T*>(&bitsk));
+#pragma unroll
+        for (int row = 0; row < RP; ++row)
+          r.v[mm * RP + row] += (unsigned long long)(long long)f2x_f32<BITS>(__fmul_rn(qf[row], kf), scale);
+      }
+    }
+  }
+  return r;
+}
+
+template <int D, int BITS, typename T>
+__global__ void __launch_bounds__(W * 32, FXPR_DQ_MINB1)
 dq_scores_kernel(const __grid_constant__ CUtensorMap kmap, const DqParams p) {
   using GE = Geo<D>;
   constexpr int ROWB = GE::ROWB, PAGEB = GE::PAGEB, CQ = GE::CQ, DPT = GE::DPT;
   extern __shared__ __align__(1024) unsigned char smem[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   unsigned char* stage0 = smem + warp * (S * PAGEB);
+  const uint32_t stage0_a = tma::smem_addr(stage0);
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + W * S * PAGEB) + warp * S;
   int* pre = reinterpret_cast<int*>(smem + W * S * PAGEB + W * S * 8);
 
@@ -243,53 +338,49 @@ dq_scores_kernel(const __grid_constant__ CUtensorMap kmap, const DqParams p) {
   __syncwarp();
   const uint64_t pol = tma::policy_evict_first();
 
-  Slot A = resolve(p, pre, G0, G1), B = resolve(p, pre, G0 + 32, G1);
-  int a_idx = 0;
+  Pipe pp;
+  pp.A = resolve(p, pre, G0, G1);
+  pp.B = resolve(p, pre, G0 + 32, G1);
+  pp.a_idx = 0;
   auto issue = [&](int i) {
-    const Slot sl = slot_of(A, B, (i >> 5) != a_idx, i & 31);
+    const int2 c = pp.coords(i);
     if (lane == 0) {
-      const int kvh = sl.item % p.KVH;
-      const int key0 = sl.pg * PG;
-      const int slot0 = p.page_shift >= 0 ? (key0 & (p.page - 1)) : key0 % p.page;
       uint64_t* bar = &bars[i % S];
       tma::fence_proxy_async();
       tma::mbar_expect_tx(bar, PAGEB);
-      tma::load_4d(stage0 + (i % S) * PAGEB, &kmap, 0, kvh, slot0, sl.blk, bar, pol);
+      tma::load_4d(stage0 + (i % S) * PAGEB, &kmap, 0, c.x & 0xFFFF, c.x >> 16, c.y, bar, pol);
     }
   };
   for (int i = 0; i < S - 1 && i < n; ++i) issue(i);
 
   const int kg = lane >> 3, kq = lane & (TPK - 1);
+  const int my_row = kq & 3, my_key = kg + 4 * (kq >> 2);  // after the reduce-scatter
+  const uint32_t lane_off = kg * ROWB + kq * 16;
   const float scale = ldexpf(1.0f, p.frac), inv_scale = ldexpf(1.0f, -p.frac);
   const float2 C2 = make_float2(kMagic, kMagic);
-  int cur_item = -1, kend = 0, tok = 0, kvh = 0;
+  int cur_item = -1, kend = 0;
+  const T* qbase = nullptr;
   float kthr = 0.0f;
   float2 qr[RP][CQ][4];  // this lane's q dims (pre-scaled by 2^f), fp32 pairs
 
   for (int i = 0; i < n; ++i) {
-    if ((i >> 5) != a_idx) {
-      A = B;
-      ++a_idx;
-      B = resolve(p, pre, G0 + (a_idx + 1) * 32, G1);
-    }
+    if ((i >> 5) != pp.a_idx) pp.advance(p, pre, G0, G1);
     if (i + S - 1 < n) issue(i + S - 1);
-    const Slot sl = slot_of(A, B, false, i & 31);
-    if (sl.item != cur_item) {
-      cur_item = sl.item;
-      const int r = sl.item / p.KVH;
-      kvh = sl.item - r * p.KVH;
-      tok = p.qsl[r];
+    const int2 ip = pp.item_pg(i);
+    if (ip.x != cur_item) {
+      cur_item = ip.x;
+      const int r = ip.x / p.KVH;
+      const int kvh = ip.x - r * p.KVH;
       const int sl_r = p.seq_lens[r];
       kend = min(sl_r, p.kmax);
       if (sl_r > p.kmax && lane == 0) atomicOr(p.err, kErrContextCut);
+      qbase = reinterpret_cast<const T*>(p.q) + (int64_t)p.qsl[r] * p.q_st + (int64_t)(kvh * RP) * p.q_sh;
       uint32_t qo = 0;
 #pragma unroll
       for (int row = 0; row < RP; ++row)
 #pragma unroll
         for (int h = 0; h < CQ; ++h) {
-          const T* src = reinterpret_cast<const T*>(p.q) + (int64_t)tok * p.q_st +
-                         (int64_t)(kvh * RP + row) * p.q_sh + (kq + TPK * h) * 8;
-          const uint4 w = *reinterpret_cast<const uint4*>(src);
+          const uint4 w = *reinterpret_cast<const uint4*>(qbase + row * p.q_sh + (kq + TPK * h) * 8);
           float2 f[4];
           unpack8<T>(w, f);
 #pragma unroll
@@ -304,29 +395,28 @@ dq_scores_kernel(const __grid_constant__ CUtensorMap kmap, const DqParams p) {
       const double mq = (double)__uint_as_float(qo) * (double)ldexp(1.0, p.frac);
       kthr = mq < 3.0e38 ? __double2float_rd(4194304.0 / mq) : 0.0f;  // NaN: 0
     }
-    if (sl.pg == 0) {  // first page of the item: clear its pv accumulators
-      unsigned long long* a = p.acc + (int64_t)sl.item * (RP * D);
+    if (ip.y == 0) {  // first page of the item: clear its pv accumulators
+      unsigned long long* a = p.acc + (int64_t)ip.x * (RP * D);
       for (int e = lane; e < RP * D; e += 32) a[e] = 0ull;
-      if (lane < RP) p.den[(int64_t)sl.item * RP + lane] = 0ull;
-      if (lane == 0) p.cnt[sl.item] = 0u;
+      if (lane < RP) p.den[(int64_t)ip.x * RP + lane] = 0ull;
+      if (lane == 0) p.cnt[ip.x] = 0u;
     }
     if (!tma::mbar_wait(&bars[i % S], (uint32_t)((i / S) & 1))) {
       if (lane == 0) atomicOr(p.err, kErrWaitTimeout);
       drain(bars, i, n);
       break;
     }
-    const unsigned char* kt = stage0 + (i % S) * PAGEB;
-    const int64_t Gp = (int64_t)G0 + i;
+    const uint32_t kt = stage0_a + (i % S) * PAGEB;
+    float* srow = p.s + ((int64_t)G0 + i) * (RP * PG) + my_row * PG;
+    const int jbase = ip.y * PG;
     float rmax = -INFINITY;
 #pragma unroll
     for (int st = 0; st < 2; ++st) {
-      const int kA = st * 8 + kg;
       uint4 w[2][CQ];
 #pragma unroll
       for (int mm = 0; mm < 2; ++mm)
 #pragma unroll
-        for (int h = 0; h < CQ; ++h)
-          w[mm][h] = *reinterpret_cast<const uint4*>(kt + (kA + 4 * mm) * ROWB + (kq + TPK * h) * 16);
+        for (int h = 0; h < CQ; ++h) w[mm][h] = lds128(kt + lane_off + (st * 8 + 4 * mm) * ROWB + h * TPK * 16);
       AbsMax16 km;
       uint32_t acc[2][RP];
 #pragma unroll
@@ -360,46 +450,29 @@ dq_scores_kernel(const __grid_constant__ CUtensorMap kmap, const DqParams p) {
         reduce_scatter8_u32(v, kq);
         dot = (long long)(int32_t)v[0];  // |fast-path dot| < 2^29
       } else {
-        // exact path: every product clamped and rounded on its own
-        unsigned long long v[8];
-#pragma unroll
-        for (int mm = 0; mm < 2; ++mm) {
-          const int key = kA + 4 * mm;
-#pragma unroll
-          for (int row = 0; row < RP; ++row) {
-            unsigned long long ex = 0ull;
-            const T* qsrc = reinterpret_cast<const T*>(p.q) + (int64_t)tok * p.q_st +
-                            (int64_t)(kvh * RP + row) * p.q_sh;
-            for (int h = 0; h < CQ; ++h) {
-              const int c = kq + TPK * h;
-              const T* kv = reinterpret_cast<const T*>(kt + key * ROWB + c * 16);
-              for (int e = 0; e < 8; ++e)
-                ex += (unsigned long long)(long long)f2x_f32<BITS>(
-                    __fmul_rn(to_f32(qsrc[c * 8 + e]), to_f32(kv[e])), scale);
-            }
-            v[mm * RP + row] = ex;
-          }
-        }
-        reduce_scatter8_u64(v, kq);
-        dot = (BITS == 64) ? (long long)v[0] : (long long)(int32_t)(uint32_t)v[0];
+        Dots8 ex = exact_dots<D, BITS, T>(qbase, p.q_sh, kt, st * 8 + kg, kq, scale);
+        reduce_scatter8_u64(ex.v, kq);
+        dot = (BITS == 64) ? (long long)ex.v[0] : (long long)(int32_t)(uint32_t)ex.v[0];
       }
-      // lane kq now holds (key kA + 4 * (kq >> 2), row kq & 3)
-      const int key = kA + 4 * (kq >> 2), row = kq & 3;
-      const int j = sl.pg * PG + key;
+      // lane kq now holds (key st * 8 + my_key, row my_row)
+      const int key = st * 8 + my_key;
       float qk = (BITS == 64) ? __ll2float_rn(dot) : __int2float_rn((int)dot);
       qk = __fmul_rn(__fmul_rn(qk, inv_scale), p.scale_log2);
-      const float sc = j < kend ? qk : -INFINITY;
-      p.s[Gp * (RP * PG) + row * PG + key] = sc;
+      const float sc = jbase + key < kend ? qk : -INFINITY;
+      srow[key] = sc;
       rmax = fmaxf(rmax, sc);
     }
     rmax = fmaxf(rmax, __shfl_xor_sync(0xffffffffu, rmax, 4));
     rmax = fmaxf(rmax, __shfl_xor_sync(0xffffffffu, rmax, 8));
     rmax = fmaxf(rmax, __shfl_xor_sync(0xffffffffu, rmax, 16));
-    if (lane < RP) p.m[Gp * RP + lane] = rmax;
+    if (lane < RP) p.m[((int64_t)G0 + i) * RP + lane] = rmax;
     __syncwarp();  // every lane is done with this page's buffer
   }
 }
 
+// ---------------------------------------------------------------------------
+// kernel 2: normaliser, PV and the integer combine
+// ---------------------------------------------------------------------------
 // DPL V elements of a key row as fp32 after the reference's cast to fp16
 // (attention.py:245-249); E16: the bf16 -> fp16 step is exact, skip it
 template <typename T, int DPL, bool E16, typename R>
@@ -424,19 +497,55 @@ __device__ __forceinline__ void v_to_f32(R r, float* f) {
   }
 }
 
-// ---------------------------------------------------------------------------
-// kernel 2: normaliser, PV and the integer combine
-// ---------------------------------------------------------------------------
+template <int DPL> struct VLoad;
+template <> struct VLoad<4> {
+  using R = uint2;
+  __device__ static __forceinline__ R ld(uint32_t a) { return lds64(a); }
+};
+template <> struct VLoad<2> {
+  using R = uint32_t;
+  __device__ static __forceinline__ R ld(uint32_t a) { return lds32(a); }
+};
+
+// exact PV partial sums of one lane over the page's keys inside the context
+// (fp16-rounded V, every product clamped and rounded on its own)
+template <int D> struct PvPart {
+  unsigned long long v[RP][D / 32];
+};
 template <int D, int BITS, typename T>
-__global__ void __launch_bounds__(W * 32, 4)
+__device__ __forceinline__ PvPart<D> exact_pv(uint32_t vt, uint32_t ps, int nvalid, int d0) {
+  constexpr int DPL = D / 32;
+  PvPart<D> r;
+#pragma unroll
+  for (int row = 0; row < RP; ++row)
+#pragma unroll
+    for (int d = 0; d < DPL; ++d) r.v[row][d] = 0ull;
+#pragma unroll 1
+  for (int k = 0; k < nvalid && k < PG; ++k) {
+    float vv[DPL];
+    v_to_f32<T, DPL, false>(VLoad<DPL>::ld(vt + k * D * 2 + d0 * 2), vv);
+#pragma unroll
+    for (int row = 0; row < RP; ++row) {
+      const float pv = __uint_as_float(lds32(ps + (row * PG + k) * 4));
+#pragma unroll
+      for (int d = 0; d < DPL; ++d)
+        r.v[row][d] += (unsigned long long)(long long)f2x_scaled<BITS>(__fmul_rn(pv, vv[d]));
+    }
+  }
+  return r;
+}
+
+template <int D, int BITS, typename T>
+__global__ void __launch_bounds__(W * 32, FXPR_DQ_MINB2)
 dq_pv_kernel(const __grid_constant__ CUtensorMap vmap, const DqParams p) {
   using GE = Geo<D>;
   constexpr int ROWB = GE::ROWB, PAGEB = GE::PAGEB, DPL = GE::DPL;
   constexpr int STB = PAGEB + RP * PG * 4;  // V page + its scores
-  using VRaw = typename std::conditional<DPL == 4, uint2, uint32_t>::type;
+  using UAcc = typename std::conditional<BITS == 64, unsigned long long, uint32_t>::type;
   extern __shared__ __align__(1024) unsigned char smem[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   unsigned char* stage0 = smem + warp * (S * STB);
+  const uint32_t stage0_a = tma::smem_addr(stage0);
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + W * S * STB) + warp * S;
   int* pre = reinterpret_cast<int*>(smem + W * S * STB + W * S * 8);
 
@@ -453,19 +562,18 @@ dq_pv_kernel(const __grid_constant__ CUtensorMap vmap, const DqParams p) {
   __syncwarp();
   const uint64_t pol = tma::policy_evict_first();
 
-  Slot A = resolve(p, pre, G0, G1), B = resolve(p, pre, G0 + 32, G1);
-  int a_idx = 0;
+  Pipe pp;
+  pp.A = resolve(p, pre, G0, G1);
+  pp.B = resolve(p, pre, G0 + 32, G1);
+  pp.a_idx = 0;
   auto issue = [&](int i) {
-    const Slot sl = slot_of(A, B, (i >> 5) != a_idx, i & 31);
+    const int2 c = pp.coords(i);
     if (lane == 0) {
-      const int kvh = sl.item % p.KVH;
-      const int key0 = sl.pg * PG;
-      const int slot0 = p.page_shift >= 0 ? (key0 & (p.page - 1)) : key0 % p.page;
       uint64_t* bar = &bars[i % S];
       unsigned char* dst = stage0 + (i % S) * STB;
       tma::fence_proxy_async();
       tma::mbar_expect_tx(bar, STB);
-      tma::load_4d(dst, &vmap, 0, kvh, slot0, sl.blk, bar, pol);
+      tma::load_4d(dst, &vmap, 0, c.x & 0xFFFF, c.x >> 16, c.y, bar, pol);
       tma::load_bulk(dst + PAGEB, p.s + ((int64_t)G0 + i) * (RP * PG), RP * PG * 4, bar);
     }
   };
@@ -481,25 +589,24 @@ dq_pv_kernel(const __grid_constant__ CUtensorMap vmap, const DqParams p) {
   const int d0 = lane * DPL;                      // pv-phase: dims of this lane
 
   int cur_item = -1, kend = 0, tok = 0, kvh = 0, np = 0, run = 0;
-  float gmax[RP];
-  unsigned long long acc[RP][DPL];
-  unsigned long long den = 0ull;  // this lane's share of row pr
+  float g_row = -INFINITY;  // max of row pr over the item
+  UAcc acc[RP][DPL];
+  UAcc den = 0;  // this lane's share of row pr
 
   // add the warp's partial sums of the current item to the output (whole
   // item) or to the item's accumulators (the last contributor finalises)
   auto flush = [&]() {
 #pragma unroll
     for (int o = 1; o < 8; o <<= 1) den += __shfl_xor_sync(0xffffffffu, den, o);
-    bool whole = run == np;
-    unsigned long long dn[RP];
-    if (!whole) {
+    UAcc dn[RP];
+    if (run != np) {
       unsigned long long* ga = p.acc + (int64_t)cur_item * (RP * D);
 #pragma unroll
       for (int row = 0; row < RP; ++row)
 #pragma unroll
         for (int d = 0; d < DPL; ++d)
-          if (acc[row][d]) atomicAdd(ga + row * D + d0 + d, acc[row][d]);
-      if ((lane & 7) == 0 && den) atomicAdd(p.den + (int64_t)cur_item * RP + pr, den);
+          if (acc[row][d]) atomicAdd(ga + row * D + d0 + d, (unsigned long long)acc[row][d]);
+      if ((lane & 7) == 0 && den) atomicAdd(p.den + (int64_t)cur_item * RP + pr, (unsigned long long)den);
       __threadfence();
       __syncwarp();
       unsigned last = 0;
@@ -510,8 +617,8 @@ dq_pv_kernel(const __grid_constant__ CUtensorMap vmap, const DqParams p) {
 #pragma unroll
       for (int row = 0; row < RP; ++row) {
 #pragma unroll
-        for (int d = 0; d < DPL; ++d) acc[row][d] = __ldcg(ga + row * D + d0 + d);
-        dn[row] = __ldcg(p.den + (int64_t)cur_item * RP + row);
+        for (int d = 0; d < DPL; ++d) acc[row][d] = (UAcc)__ldcg(ga + row * D + d0 + d);
+        dn[row] = (UAcc)__ldcg(p.den + (int64_t)cur_item * RP + row);
       }
     } else {
 #pragma unroll
@@ -521,57 +628,52 @@ dq_pv_kernel(const __grid_constant__ CUtensorMap vmap, const DqParams p) {
     for (int row = 0; row < RP; ++row) {
       float df;
       if constexpr (BITS == 64) df = __fmul_rn(__ll2float_rn((long long)dn[row]), inv_scale);
-      else df = __fmul_rn(__int2float_rn((int32_t)(uint32_t)dn[row]), inv_scale);
+      else df = __fmul_rn(__int2float_rn((int32_t)dn[row]), inv_scale);
       const float dsafe = fmaxf(df, 1.0e-6f);
       const int64_t ob = (int64_t)tok * p.o_st + (int64_t)(kvh * RP + row) * p.o_sh + d0;
 #pragma unroll
       for (int d = 0; d < DPL; ++d) {
         float af;
         if constexpr (BITS == 64) af = __fmul_rn(__ll2float_rn((long long)acc[row][d]), inv_scale);
-        else af = __fmul_rn(__int2float_rn((int32_t)(uint32_t)acc[row][d]), inv_scale);
+        else af = __fmul_rn(__int2float_rn((int32_t)acc[row][d]), inv_scale);
         store_f32(p.o, p.o_dtype, ob + d, prim_div(af, dsafe));
       }
     }
   };
 
   for (int i = 0; i < n; ++i) {
-    if ((i >> 5) != a_idx) {
-      A = B;
-      ++a_idx;
-      B = resolve(p, pre, G0 + (a_idx + 1) * 32, G1);
-    }
+    if ((i >> 5) != pp.a_idx) pp.advance(p, pre, G0, G1);
     if (i + S - 1 < n) issue(i + S - 1);
-    const Slot sl = slot_of(A, B, false, i & 31);
-    if (sl.item != cur_item) {
+    const int2 ip = pp.item_pg(i);
+    if (ip.x != cur_item) {
       if (cur_item >= 0) flush();
-      cur_item = sl.item;
-      const int r = sl.item / p.KVH;
-      kvh = sl.item - r * p.KVH;
+      cur_item = ip.x;
+      const int r = ip.x / p.KVH;
+      kvh = ip.x - r * p.KVH;
       tok = p.qsl[r];
       kend = min(p.seq_lens[r], p.kmax);
       np = (pre[r + 1] - pre[r]) / p.KVH;
       run = 0;
-      den = 0ull;
+      den = 0;
 #pragma unroll
       for (int row = 0; row < RP; ++row)
 #pragma unroll
-        for (int d = 0; d < DPL; ++d) acc[row][d] = 0ull;
+        for (int d = 0; d < DPL; ++d) acc[row][d] = 0;
       // the item's row maxima: max over its pages
       const int64_t P0 = (int64_t)pre[r] + (int64_t)kvh * np;
-#pragma unroll
-      for (int row = 0; row < RP; ++row) gmax[row] = -INFINITY;
+      float gm[RP] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
       for (int k = lane; k < np; k += 32) {
         const float4 mx = *reinterpret_cast<const float4*>(p.m + (P0 + k) * RP);
-        gmax[0] = fmaxf(gmax[0], mx.x);
-        gmax[1] = fmaxf(gmax[1], mx.y);
-        gmax[2] = fmaxf(gmax[2], mx.z);
-        gmax[3] = fmaxf(gmax[3], mx.w);
+        gm[0] = fmaxf(gm[0], mx.x);
+        gm[1] = fmaxf(gm[1], mx.y);
+        gm[2] = fmaxf(gm[2], mx.z);
+        gm[3] = fmaxf(gm[3], mx.w);
       }
 #pragma unroll
       for (int row = 0; row < RP; ++row)
 #pragma unroll
-        for (int o = 1; o < 32; o <<= 1)
-          gmax[row] = fmaxf(gmax[row], __shfl_xor_sync(0xffffffffu, gmax[row], o));
+        for (int o = 1; o < 32; o <<= 1) gm[row] = fmaxf(gm[row], __shfl_xor_sync(0xffffffffu, gm[row], o));
+      g_row = pr == 0 ? gm[0] : pr == 1 ? gm[1] : pr == 2 ? gm[2] : gm[3];
     }
     if (!tma::mbar_wait(&bars[i % S], (uint32_t)((i / S) & 1))) {
       if (lane == 0) atomicOr(p.err, kErrWaitTimeout);
@@ -580,18 +682,18 @@ dq_pv_kernel(const __grid_constant__ CUtensorMap vmap, const DqParams p) {
       break;
     }
     ++run;
-    unsigned char* vt = stage0 + (i % S) * STB;
-    float* ps = reinterpret_cast<float*>(vt + PAGEB);  // [RP][PG] score -> p * 2^f
+    const uint32_t vt = stage0_a + (i % S) * STB;
+    const uint32_t ps = vt + PAGEB;  // [RP][PG] score -> p * 2^f
+    const int jbase = ip.y * PG;
     // ---- p = exp2(score - max) for keys inside the context (attention.py:237-243) ----
     {
-      const float2 sc = *reinterpret_cast<const float2*>(ps + pr * PG + pk);
-      const int j = sl.pg * PG + pk;
-      const float g_row = pr == 0 ? gmax[0] : pr == 1 ? gmax[1] : pr == 2 ? gmax[2] : gmax[3];
-      const float p0 = j < kend ? prim_exp2(__fsub_rn(sc.x, g_row)) : 0.0f;
-      const float p1 = j + 1 < kend ? prim_exp2(__fsub_rn(sc.y, g_row)) : 0.0f;
-      den += (unsigned long long)(long long)f2x_f32<BITS>(p0, scale);
-      den += (unsigned long long)(long long)f2x_f32<BITS>(p1, scale);
-      *reinterpret_cast<float2*>(ps + pr * PG + pk) = make_float2(__fmul_rn(p0, scale), __fmul_rn(p1, scale));
+      const uint32_t a = ps + (pr * PG + pk) * 4;
+      const uint2 sc = lds64(a);
+      const int j = jbase + pk;
+      const float p0 = j < kend ? prim_exp2(__fsub_rn(__uint_as_float(sc.x), g_row)) : 0.0f;
+      const float p1 = j + 1 < kend ? prim_exp2(__fsub_rn(__uint_as_float(sc.y), g_row)) : 0.0f;
+      den += (UAcc)f2x_f32<BITS>(p0, scale) + (UAcc)f2x_f32<BITS>(p1, scale);
+      sts64f(a, __fmul_rn(p0, scale), __fmul_rn(p1, scale));
     }
     __syncwarp();
     // ---- PV (attention.py:245-255): acc[row][d] += F2X(p * fp16(v)) ----
@@ -601,16 +703,17 @@ dq_pv_kernel(const __grid_constant__ CUtensorMap vmap, const DqParams p) {
 #pragma unroll
       for (int d = 0; d < DPL; ++d) tv[row][d] = 0u;
     AbsMax16 vm;
+    const uint32_t vlane = vt + d0 * 2;
     auto pv_page = [&](auto e16) {
 #pragma unroll
       for (int k4 = 0; k4 < PG; k4 += 4) {
-        float4 pp4[RP];
+        float4 p4[RP];
 #pragma unroll
-        for (int row = 0; row < RP; ++row) pp4[row] = *reinterpret_cast<const float4*>(ps + row * PG + k4);
+        for (int row = 0; row < RP; ++row) p4[row] = lds128f(ps + (row * PG + k4) * 4);
 #pragma unroll
         for (int h2 = 0; h2 < 4; h2 += 2) {
-          const VRaw ra = *reinterpret_cast<const VRaw*>(vt + (k4 + h2) * ROWB + d0 * 2);
-          const VRaw rb = *reinterpret_cast<const VRaw*>(vt + (k4 + h2 + 1) * ROWB + d0 * 2);
+          const auto ra = VLoad<DPL>::ld(vlane + (k4 + h2) * ROWB);
+          const auto rb = VLoad<DPL>::ld(vlane + (k4 + h2 + 1) * ROWB);
           if constexpr (DPL == 4) {
             vm.add2(ra.x, ra.y);
             vm.add2(rb.x, rb.y);
@@ -622,10 +725,10 @@ dq_pv_kernel(const __grid_constant__ CUtensorMap vmap, const DqParams p) {
           v_to_f32<T, DPL, decltype(e16)::value>(rb, vb);
 #pragma unroll
           for (int row = 0; row < RP; ++row) {
-            const float2 pp = h2 == 0 ? make_float2(pp4[row].x, pp4[row].y) : make_float2(pp4[row].z, pp4[row].w);
+            const float2 pq = h2 == 0 ? make_float2(p4[row].x, p4[row].y) : make_float2(p4[row].z, p4[row].w);
 #pragma unroll
             for (int d = 0; d < DPL; ++d) {
-              const float2 r2 = fma2(mul2(pp, make_float2(va[d], vb[d])), ONE2, C2);
+              const float2 r2 = fma2(mul2(pq, make_float2(va[d], vb[d])), ONE2, C2);
               tv[row][d] += __float_as_uint(r2.x) + __float_as_uint(r2.y);
             }
           }
@@ -640,30 +743,13 @@ dq_pv_kernel(const __grid_constant__ CUtensorMap vmap, const DqParams p) {
       for (int row = 0; row < RP; ++row)
 #pragma unroll
         for (int d = 0; d < DPL; ++d)
-          acc[row][d] += (unsigned long long)(long long)(int32_t)(tv[row][d] - (uint32_t)PG * (uint32_t)kMagicBits);
+          acc[row][d] += (UAcc)(long long)(int32_t)(tv[row][d] - (uint32_t)PG * (uint32_t)kMagicBits);
     } else {
-      // exact path: keys inside the context only, each product clamped alone
-      for (int k = 0; k < PG; ++k) {
-        if (sl.pg * PG + k >= kend) continue;
-        const VRaw rv = *reinterpret_cast<const VRaw*>(vt + k * ROWB + d0 * 2);
-        uint32_t w[DPL / 2];
-        if constexpr (DPL == 4) {
-          w[0] = rv.x;
-          w[1] = rv.y;
-        } else {
-          w[0] = rv;
-        }
+      const PvPart<D> ex = exact_pv<D, BITS, T>(vt, ps, kend - jbase, d0);
 #pragma unroll
-        for (int kk = 0; kk < DPL / 2; ++kk) {
-          const float2 vv = v_pair_f16<T>(reinterpret_cast<const unsigned char*>(&w[kk]));
+      for (int row = 0; row < RP; ++row)
 #pragma unroll
-          for (int row = 0; row < RP; ++row) {
-            const float pv = ps[row * PG + k];
-            acc[row][2 * kk] += (unsigned long long)(long long)f2x_scaled<BITS>(__fmul_rn(pv, vv.x));
-            acc[row][2 * kk + 1] += (unsigned long long)(long long)f2x_scaled<BITS>(__fmul_rn(pv, vv.y));
-          }
-        }
-      }
+        for (int d = 0; d < DPL; ++d) acc[row][d] += (UAcc)ex.v[row][d];
     }
     __syncwarp();  // every lane is done with this page's buffer
   }
