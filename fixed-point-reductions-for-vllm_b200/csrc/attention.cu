@@ -300,10 +300,10 @@ __global__ void __launch_bounds__(THREADS) attn_kernel(Params p) {
         float qk = (BITS == 64) ? __ll2float_rn(di) : __int2float_rn((int)di);
         qk = __fmul_rn(__fmul_rn(qk, inv_scale), p.scale_log2);
         if (p.softcap_log2 > 0.0f)
-          qk = __fmul_rn(p.softcap_log2, prim_tanh(prim_div(qk, p.softcap_log2)));
+          qk = __fmul_rn(p.softcap_log2, prim_tanh(__fmul_rn(qk, p.softcap_rcp)));
         const int pos = row_pos[i];
         if (p.alibi)
-          qk = __fadd_rn(qk, __fmul_rn(p.alibi[row_head[i]], __fsub_rn((float)j, (float)pos)));
+          qk = __fmaf_rn(p.alibi[row_head[i]], __fsub_rn((float)j, (float)pos), qk);  // contracted, as Triton lowers it
         bool ok = true;
         if (p.causal) ok = ok && (pos >= j);
         if (p.window > 0) ok = ok && (j > pos - p.window);
@@ -763,6 +763,7 @@ extern "C" int fxpr_unified_attention_fxp(const fxpr_attention_params* a, void* 
   p.head_slices = pl.head_slices; p.qt = pl.qt; p.page = a->page_size;
   p.causal = a->is_causal; p.window = a->window_size;
   p.scale_log2 = a->scale_log2; p.softcap_log2 = a->logits_soft_cap;
+  p.softcap_rcp = a->logits_soft_cap > 0.0f ? 1.0f / a->logits_soft_cap : 0.0f;
   p.frac = a->frac_bits;
   p.exact_qk = (a->q_dtype != FXPR_F32) && (a->kv_dtype != FXPR_F32);
   p.qtiles = pl.qtiles;

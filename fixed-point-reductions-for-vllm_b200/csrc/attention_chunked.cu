@@ -186,8 +186,8 @@ __device__ __forceinline__ float score_of(const Params& p, long long di, int j, 
   qk = __fmul_rn(__fmul_rn(qk, inv_scale), p.scale_log2);
   bool ok = j < kend;
   if constexpr (!PL) {
-    if (p.softcap_log2 > 0.0f) qk = __fmul_rn(p.softcap_log2, prim_tanh(prim_div(qk, p.softcap_log2)));
-    if (p.alibi) qk = __fadd_rn(qk, __fmul_rn(p.alibi[head], __fsub_rn((float)j, (float)pos)));
+    if (p.softcap_log2 > 0.0f) qk = __fmul_rn(p.softcap_log2, prim_tanh(__fmul_rn(qk, p.softcap_rcp)));
+    if (p.alibi) qk = __fmaf_rn(p.alibi[head], __fsub_rn((float)j, (float)pos), qk);  // contracted, as Triton lowers it
     if (p.window > 0) ok = ok && (j > pos - p.window);
   }
   if (p.causal) ok = ok && (pos >= j);

@@ -38,6 +38,7 @@ struct Params {
   int num_heads, num_kv_heads, group, gs, head_slices, qt, page;
   int causal, window;
   float scale_log2, softcap_log2;
+  float softcap_rcp;  // RN(1 / softcap_log2): Triton folds the division by the constant cap
   int frac;
   int exact_qk;  // q and K are 16-bit floats: products are exact in fp32
   int cap;       // score capacity (keys) per CTA

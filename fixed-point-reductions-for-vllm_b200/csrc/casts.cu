@@ -137,6 +137,97 @@ __global__ void __launch_bounds__(256) fxp_sum_kernel(const T* __restrict__ x, i
   }
 }
 
+// Vectorised bf16 / fp32 variant: F2X by the magic-constant rounding, two
+// elements per packed FMA (x * 2^f is exact, so one rounding = RNE), integer
+// sums of the bit patterns. A thread whose elements all satisfy
+// |x| * 2^f < 2^22 (int16: < 32767.5, inside the clamp range) is exact on the
+// fast path; a thread with a larger, inf or NaN element recomputes its own
+// elements with the clamp-and-convert path. Both give the same bits.
+template <int BITS, typename T>
+__global__ void __launch_bounds__(256) fxp_sum_magic_kernel(const T* __restrict__ x, int64_t cols,
+                                                            int64_t stride, float* __restrict__ out,
+                                                            int frac, float thr) {
+  constexpr int VEC = 16 / sizeof(T);
+  const int64_t row = blockIdx.x;
+  const T* xr = x + row * stride;
+  const uint4* xv = reinterpret_cast<const uint4*>(xr);
+  const int64_t nv = cols / VEC;
+  const float scale = ldexpf(1.0f, frac);
+  const float2 S2 = make_float2(scale, scale), C2 = make_float2(kMagic, kMagic);
+  long long acc = 0;
+  uint32_t m_u = 0, m_s = 0x80008000u;  // |x| bound of 16-bit elements (raw halves)
+  uint32_t m32 = 0;                     // |x| bound of fp32 elements (bit patterns)
+  auto take = [&](uint4 w) {
+    const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+    uint32_t part = 0;
+    if constexpr (sizeof(T) == 2) {
+      m_u = __vimax3_u16x2(m_u, w.x, w.y);
+      m_u = __vimax3_u16x2(m_u, w.z, w.w);
+      m_s = (uint32_t)__vimax3_s16x2((int)m_s, (int)w.x, (int)w.y);
+      m_s = (uint32_t)__vimax3_s16x2((int)m_s, (int)w.z, (int)w.w);
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const float2 f = make_float2(__uint_as_float(ws[k] << 16), __uint_as_float(ws[k] & 0xFFFF0000u));
+        const float2 r = fma2(f, S2, C2);
+        part += __float_as_uint(r.x) + __float_as_uint(r.y);
+      }
+      part -= (uint32_t)8 * (uint32_t)kMagicBits;
+    } else {
+      m32 = max(max(m32, ws[0] & 0x7FFFFFFFu), ws[1] & 0x7FFFFFFFu);
+      m32 = max(max(m32, ws[2] & 0x7FFFFFFFu), ws[3] & 0x7FFFFFFFu);
+#pragma unroll
+      for (int k = 0; k < 4; k += 2) {
+        const float2 r = fma2(make_float2(__uint_as_float(ws[k]), __uint_as_float(ws[k + 1])), S2, C2);
+        part += __float_as_uint(r.x) + __float_as_uint(r.y);
+      }
+      part -= (uint32_t)4 * (uint32_t)kMagicBits;
+    }
+    acc += (long long)(int32_t)part;  // |part| <= 8 * 2^22
+  };
+  int64_t i = threadIdx.x;
+  for (; i + 3 * (int64_t)blockDim.x < nv; i += 4 * (int64_t)blockDim.x) {
+    uint4 t[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) t[k] = __ldcs(xv + i + k * blockDim.x);
+#pragma unroll
+    for (int k = 0; k < 4; ++k) take(t[k]);
+  }
+  for (; i < nv; i += blockDim.x) take(__ldcs(xv + i));
+  float mx;
+  if constexpr (sizeof(T) == 2) {
+    const uint32_t pk = __vmaxu2(m_u & 0x7FFF7FFFu, m_s & 0x7FFF7FFFu);
+    mx = __uint_as_float(max(pk & 0xFFFFu, pk >> 16) << 16);
+  } else {
+    mx = __uint_as_float(m32);
+  }
+  if (!(mx < thr)) {  // this thread's vectors again, each element clamped alone
+    acc = 0;
+    for (int64_t v = threadIdx.x; v < nv; v += blockDim.x)
+      for (int e = 0; e < VEC; ++e) acc += (long long)f2x_f32<BITS>(to_f32(xr[v * VEC + e]), scale);
+  }
+  for (int64_t k = nv * VEC + threadIdx.x; k < cols; k += blockDim.x)
+    acc += (long long)f2x_f32<BITS>(to_f32(xr[k]), scale);
+  // integer block reduction (exact, order-free)
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+  __shared__ long long red[32];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (lane == 0) red[warp] = acc;
+  __syncthreads();
+  if (warp == 0) {
+    acc = (lane < (int)(blockDim.x >> 5)) ? red[lane] : 0;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+    if (lane == 0) {
+      if (BITS < 64) {
+        const long long hi = (1LL << (BITS - 1)) - 1, lo = -(1LL << (BITS - 1));
+        acc = acc > hi ? hi : (acc < lo ? lo : acc);
+      }
+      out[row] = __fmul_rn(__ll2float_rn(acc), ldexpf(1.0f, -frac));
+    }
+  }
+}
+
 template <int BITS>
 static int launch_fxp_sum(const void* x, int dtype, int64_t rows, int64_t cols, int64_t stride,
                           float* out, int frac, cudaStream_t st) {
@@ -147,6 +238,16 @@ static int launch_fxp_sum(const void* x, int dtype, int64_t rows, int64_t cols, 
   int threads = (int)(((nvec + 4 * 32 - 1) / (4 * 32)) * 32);
   threads = threads < 64 ? 64 : (threads > 256 ? 256 : threads);
   const dim3 grid((unsigned)rows), block(threads);
+  // |x| bound of the magic-constant path: |x| * 2^f below 2^22 (int16: inside
+  // the clamp range), as an fp32 threshold on |x|
+  const float thr = (float)ldexp(BITS == 16 ? 32767.5 : 4194304.0, -frac);
+  if (aligned && frac <= 100 && (dtype == FXPR_BF16 || dtype == FXPR_F32)) {
+    if (dtype == FXPR_BF16)
+      fxp_sum_magic_kernel<BITS, __nv_bfloat16><<<grid, block, 0, st>>>((const __nv_bfloat16*)x, cols, stride, out, frac, thr);
+    else
+      fxp_sum_magic_kernel<BITS, float><<<grid, block, 0, st>>>((const float*)x, cols, stride, out, frac, thr);
+    return check_launch("fxpr_fxp_sum");
+  }
   switch (dtype) {
     case FXPR_BF16:
       if (aligned)

@@ -150,11 +150,51 @@ class Prims:
     tanh: Callable[[torch.Tensor], torch.Tensor]
     exp: Callable[[torch.Tensor], torch.Tensor]
     log: Callable[[torch.Tensor], torch.Tensor]
+    # c + a * b of the ALiBi term (attention.py:131-135, 204-208): the Triton
+    # interpreter rounds the product and the sum separately; Triton 3.6 on the
+    # GPU contracts them into one fused multiply-add
+    muladd: Callable[[torch.Tensor, torch.Tensor, torch.Tensor], torch.Tensor] = None
+    # qk / cap of the softcap (attention.py:130, 203), cap a compile-time
+    # constant: the interpreter divides; Triton 3.6 on the GPU multiplies by
+    # the fp32 reciprocal of the constant
+    div_const: Callable[[torch.Tensor, torch.Tensor], torch.Tensor] = None
+
+
+def _muladd_separate(a: torch.Tensor, b: torch.Tensor, c: torch.Tensor) -> torch.Tensor:
+    return c + a * b
+
+
+def mul_rcp32(a: torch.Tensor, c: torch.Tensor) -> torch.Tensor:
+    """a / c as the GPU build of the reference computes it for a constant c:
+    a * RN(1 / c) in fp32."""
+    rc = torch.tensor(1.0, dtype=torch.float32) / c.to(torch.float32)
+    return a.to(torch.float32) * rc
+
+
+def fma32(a: torch.Tensor, b: torch.Tensor, c: torch.Tensor) -> torch.Tensor:
+    """Correctly rounded fp32 fused multiply-add RN(a * b + c), computed in
+    float64: the product of two fp32 values is exact in float64; the sum is
+    split by TwoSum into s + e exactly, and s is rounded to fp32 with e
+    deciding only when s sits exactly on an fp32 rounding midpoint."""
+    a64, b64, c64 = (torch.broadcast_tensors(a.double(), b.double(), c.double()))
+    x = a64 * b64
+    s = x + c64
+    bb = s - x
+    e = (x - (s - bb)) + (c64 - bb)  # s + e == x + c exactly
+    r = s.to(torch.float32)
+    lo = torch.nextafter(r, torch.full_like(r, -float("inf")))
+    hi = torch.nextafter(r, torch.full_like(r, float("inf")))
+    # s exactly halfway between r and a neighbour: e picks the side
+    up_mid = (r.double() + hi.double()) / 2 == s
+    dn_mid = (r.double() + lo.double()) / 2 == s
+    r = torch.where(up_mid & (e > 0), hi, r)
+    r = torch.where(dn_mid & (e < 0), lo, r)
+    return torch.where(torch.isfinite(s), r, (a * b + c))
 
 
 NUMPY_PRIMS = Prims(
     exp2=_np_unary(np.exp2), div=_np_div, sqrt=_np_unary(np.sqrt), tanh=_np_unary(np.tanh),
-    exp=_np_unary(np.exp), log=_np_unary(np.log),
+    exp=_np_unary(np.exp), log=_np_unary(np.log), muladd=_muladd_separate,
 )
 
 
@@ -353,10 +393,11 @@ def unified_attention_fxp(q, kv_cache, o, query_start_loc, seq_lens, block_table
                 s_int = wrap_int(float_to_fixed(prod, frac_bits, int_bits).to(torch.int64).sum(-1), int_bits)
                 qk = fixed_to_float(s_int, frac_bits, torch.float32) * scale32
                 if logits_soft_cap > 0.0:
-                    qk = cap_log2 * prims.tanh(prims.div(qk, cap_log2))
+                    qk = cap_log2 * prims.tanh((prims.div_const or prims.div)(qk, cap_log2))
                 if alibi_slopes is not None:
                     slope = alibi_slopes[h].to(torch.float32)
-                    qk = qk + slope * (keys[None, :].to(torch.float32) - pos[:, None].to(torch.float32))
+                    diff = keys[None, :].to(torch.float32) - pos[:, None].to(torch.float32)
+                    qk = (prims.muladd or _muladd_separate)(slope, diff, qk)
                 mask = torch.ones((len(qoffs), len(keys)), dtype=torch.bool)
                 if is_causal:
                     mask &= pos[:, None] >= keys[None, :]

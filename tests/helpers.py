@@ -35,6 +35,8 @@ def device_prims(device="cuda") -> O.Prims:
         tanh=lambda x: run(3, x),
         exp=lambda x: run(4, x),
         log=lambda x: run(5, x),
+        muladd=O.fma32,  # Triton on the GPU contracts the ALiBi multiply-add
+        div_const=O.mul_rcp32,  # and divides by the constant softcap via its reciprocal
     )
 
 

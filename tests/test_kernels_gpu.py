@@ -81,6 +81,27 @@ def test_fxp_sum(bits, dtype):
         assert torch.equal(got, O.fxp_sum(x, f, bits))
 
 
+@pytest.mark.parametrize("bits", [16, 32, 64])
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+def test_fxp_sum_vector_path(bits, dtype):
+    """16-byte aligned rows take the vectorised magic-constant path: rows with
+    a ragged tail (strided view), rows whose values force the exact path
+    (large, inf, NaN) next to rows that do not."""
+    from fxpr_vllm.fixed_point_kernels import fixed_point as F
+
+    g = torch.Generator().manual_seed(11 + bits)
+    base = (torch.randn(40, 1032, generator=g) * 3).to(dtype)
+    base[3, 17] = 1e6
+    base[5, 1000] = float("inf")
+    base[7, 2] = float("-inf")
+    base[9, 500] = float("nan")
+    base[11, :] = 2.0 ** 14  # saturates every width's row sum
+    f = 4 if bits == 16 else 16
+    for view in (base, base[:, :1001], base[:, :8]):
+        got = F.fxp_sum(view.cuda(), f, bits).cpu()
+        assert torch.equal(got, O.fxp_sum(view, f, bits)), (view.shape, bits, dtype)
+
+
 def test_fxp_sum_saturation_and_order():
     from fxpr_vllm.fixed_point_kernels import fixed_point as F
 
