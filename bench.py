@@ -12,6 +12,16 @@ metric = algorithmic HBM bytes of the step / step time (GB/s), whole job
 (N GPUs run N independent shards: weak scaling, no collective).
 Inputs (1.3 GB per step) are larger than the 126 MB L2, so no explicit flush.
 
+Two more measurements ride in the same JSON line:
+
+* ``tp_layer``: one Llama-3-8B-architecture decode layer at tensor
+  parallelism N (all ranks), whose row-parallel partials are summed as int64
+  by NCCL before X2F: time per layer (max over ranks), the allreduce share,
+  the implied 32-layer decode tokens/s, and a checksum of the output bits
+  that is the same for every N;
+* ``device_baseline``: the reference's own Triton kernels, compiled for
+  sm_100 into oracle/_ref/, timed on the same GPU and inputs (N=1).
+
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
 ``--impl reference`` times the reference's own CPU implementation of the
@@ -154,6 +164,182 @@ class Step:
             ev[i].record()
             fn()
         ev[len(fns)].record()
+
+
+# ---------------------------------------------------------------- TP layer
+class TPLayer:
+    """One Llama-3-8B-architecture decode layer at tensor parallelism N (this
+    rank's shard): 256 tokens (one per sequence), 1024-token contexts in a
+    paged cache (page 16), int64 accumulators, f=16, random N(0, 0.02) weights
+    drawn from one seed so that every TP degree holds slices of the same
+    matrices. Column-parallel QKV and gate_up GEMMs, attention over this
+    rank's KV heads, row-parallel o_proj and down GEMMs whose raw integer
+    partials are summed by one NCCL int64 allreduce each, then X2F, the
+    residual adds and the fixed-point RMSNorms. RoPE and the KV-cache write
+    are left out (neither is a reduction). The output is bitwise independent
+    of N; ``digest()`` is a checksum of its bits."""
+
+    H, KVH, D, HID, FFN, TOK, CTX, PAGE = 32, 8, 128, 4096, 14336, 256, 1024, 16
+    BITS = 64
+
+    def __init__(self, ws: int, rank: int, device):
+        from fxpr_vllm import library_ops  # noqa: F401
+
+        assert self.KVH % ws == 0, "TP degree must divide the 8 KV heads"
+        self.ws, self.rank, self.dev = ws, rank, device
+        g = torch.Generator(device=device)
+
+        def w(seed, rows, cols):
+            g.manual_seed(seed)
+            return (torch.randn(rows, cols, generator=g, device=device) * 0.02).to(torch.bfloat16)
+
+        h, kvh, D = self.H // ws, self.KVH // ws, self.D
+        f = self.FFN // ws
+        qkv = w(11, (self.H + 2 * self.KVH) * D, self.HID)
+        q_rows = qkv[: self.H * D].view(self.H, D, -1)[rank * h:(rank + 1) * h].reshape(h * D, -1)
+        k_rows = qkv[self.H * D:(self.H + self.KVH) * D].view(self.KVH, D, -1)[rank * kvh:(rank + 1) * kvh]
+        v_rows = qkv[(self.H + self.KVH) * D:].view(self.KVH, D, -1)[rank * kvh:(rank + 1) * kvh]
+        self.w_qkv = torch.cat([q_rows, k_rows.reshape(kvh * D, -1), v_rows.reshape(kvh * D, -1)]).contiguous()
+        del qkv
+        self.w_o = w(12, self.HID, self.H * D)[:, rank * h * D:(rank + 1) * h * D].contiguous()
+        gu = w(13, 2 * self.FFN, self.HID)
+        self.w_gu = torch.cat([gu[rank * f:(rank + 1) * f], gu[self.FFN + rank * f:self.FFN + (rank + 1) * f]]).contiguous()
+        del gu
+        self.w_d = w(14, self.HID, self.FFN)[:, rank * f:(rank + 1) * f].contiguous()
+        self.norm1 = (1 + 0.1 * torch.randn(self.HID, generator=g.manual_seed(15), device=device)).to(torch.bfloat16)
+        self.norm2 = (1 + 0.1 * torch.randn(self.HID, generator=g.manual_seed(16), device=device)).to(torch.bfloat16)
+        self.x = torch.randn(self.TOK, self.HID, generator=g.manual_seed(17), device=device).to(torch.bfloat16)
+        self.res0 = torch.randn(self.TOK, self.HID, generator=g.manual_seed(18), device=device).to(torch.bfloat16)
+        # paged KV cache of this rank's KV heads: sequence s owns blocks s*64 .. s*64+63
+        nb = self.TOK * self.CTX // self.PAGE
+        kv = torch.empty(nb, 2, self.PAGE, kvh, D, dtype=torch.bfloat16, device=device)
+        g.manual_seed(19)
+        for i in range(0, nb, 1024):
+            full = torch.randn(min(1024, nb - i), 2, self.PAGE, self.KVH, D, generator=g, device=device)
+            kv[i:i + 1024] = full[:, :, :, rank * kvh:(rank + 1) * kvh].to(torch.bfloat16)
+        self.kv = kv
+        self.bt = torch.arange(nb, dtype=torch.int32, device=device).view(self.TOK, -1)
+        self.seq_lens = torch.full((self.TOK,), self.CTX, dtype=torch.int32, device=device)
+        self.qsl = torch.arange(self.TOK + 1, dtype=torch.int32, device=device)
+        self.h, self.kvh = h, kvh
+        self.o = torch.empty(self.TOK, h, D, dtype=torch.bfloat16, device=device)
+        self.ar_events = []
+
+    def _allreduce(self, t, ev=None):
+        if self.ws > 1:
+            if ev is not None:
+                ev[0].record()
+            torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.SUM)
+            if ev is not None:
+                ev[1].record()
+        return t
+
+    def step(self, ev=None):
+        from fxpr_vllm.fixed_point_kernels import attention as A
+
+        F, B = FRAC, self.BITS
+        op = torch.ops.fxpr
+        res = self.res0.clone()
+        h1 = op.rms_norm_fxp_residual(self.x, res, self.norm1, 1e-5, F, B)
+        qkv = op.fixed_to_float_bias(op.gemm_fxp_int(h1, self.w_qkv.t(), F, B), None, F, B, torch.bfloat16)
+        q = qkv[:, : self.h * self.D].view(self.TOK, self.h, self.D)
+        A.unified_attention_fxp(q, self.kv, self.o, self.qsl, self.seq_lens, self.bt, 1, fxp_dtype=B,
+                                frac_bits=F, max_seq_len=self.CTX)
+        part = op.gemm_fxp_int(self.o.view(self.TOK, -1), self.w_o.t(), F, B)
+        attn_out = op.fixed_to_float_bias(self._allreduce(part, ev[0] if ev else None), None, F, B,
+                                          torch.bfloat16)
+        h2 = op.rms_norm_fxp_residual(attn_out, res, self.norm2, 1e-5, F, B)
+        gu = op.fixed_to_float_bias(op.gemm_fxp_int(h2, self.w_gu.t(), F, B), None, F, B, torch.bfloat16)
+        f = gu.shape[1] // 2
+        act = torch.nn.functional.silu(gu[:, :f]) * gu[:, f:]
+        part = op.gemm_fxp_int(act, self.w_d.t(), F, B)
+        out = op.fixed_to_float_bias(self._allreduce(part, ev[1] if ev else None), None, F, B,
+                                     torch.bfloat16)
+        self.out = out + res
+        return self.out
+
+    def digest(self) -> str:
+        import hashlib
+
+        return hashlib.sha256(self.out.view(torch.int16).cpu().numpy().tobytes()).hexdigest()[:16]
+
+
+def run_tp_layer(ws, rank, dev, steps=10, warmup=3):
+    """Time TPLayer.step (max over ranks) and the share of its two
+    allreduces; returns the JSON object or None."""
+    layer = TPLayer(ws, rank, dev)
+    for _ in range(warmup):
+        layer.step()
+    torch.cuda.synchronize()
+    if ws > 1:
+        torch.distributed.barrier()
+    evs = [[[torch.cuda.Event(enable_timing=True) for _ in range(2)] for _ in range(2)]
+           for _ in range(steps)]
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for k in range(steps):
+        layer.step(evs[k])
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / steps
+    ar_ms = 0.0
+    if ws > 1:
+        ar_ms = sum(a.elapsed_time(b) for e in evs for a, b in e) / steps
+    t = torch.tensor([ms, ar_ms], device=dev)
+    if ws > 1:
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+    ms, ar_ms = float(t[0]), float(t[1])
+    digest = layer.digest()
+    del layer
+    torch.cuda.empty_cache()
+    return {"workload": "Llama-3-8B decode layer, 256 tokens x 1024-token context, int64 Q47.16, "
+                        f"TP={ws} (2 NCCL int64 allreduces of 256x4096)",
+            "ms_per_layer": round(ms, 4), "allreduce_ms": round(ar_ms, 4),
+            "allreduce_share": round(ar_ms / ms, 4) if ms > 0 else None,
+            "decode_tok_s_32_layers": round(TPLayer.TOK / (32 * ms / 1e3), 1),
+            "output_sha256_16": digest}
+
+
+# ---------------------------------------------------------------- device baseline
+def device_baseline(inp, dev, reps=10):
+    """The reference plugin's own Triton kernels (compiled ahead of time for
+    sm_100 into oracle/_ref/ by oracle/build_ref.py) timed on this GPU on the
+    same inputs: attention, RMSNorm and GEMM as the reference launches them
+    (fp32 RMSNorm rows, as its glue passes them). None when not built."""
+    try:
+        from oracle import ref_triton as RT
+    except Exception:
+        return None
+    if not (RT.available("attn_d128_g4_i32") and RT.available("gemm_bf16_i32")):
+        return None
+    d = {k: v.to(dev) for k, v in inp.items()}
+    from fxpr_vllm.fixed_point_kernels import attention as A
+
+    o = torch.empty(d["Q"].shape, dtype=torch.float32, device=dev)
+    x32, w32 = d["X"].float(), d["Wn"].float()
+    y32 = torch.empty_like(x32)
+    wt = d["W"].t().contiguous()
+    c = torch.empty(d["A"].shape[0], wt.shape[1], dtype=torch.float32, device=dev)
+    scale = A.prepare_log2_softmax_scale(128)
+    ops = {
+        "attention": lambda: RT.attention("attn_d128_g4_i32", d["Q"], d["KV"], o, d["qsl"],
+                                          d["seq_lens"], d["bt"], 1, scale),
+        "rms_norm": lambda: RT.rms_norm("rms_h4096_i32_r0_eps1e-06", x32, w32, y32),
+        "gemm": lambda: RT.gemm("gemm_bf16_i32", d["A"], wt, c),
+    }
+    out = {}
+    for name, fn in ops.items():
+        fn()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(reps):
+            fn()
+        e1.record()
+        torch.cuda.synchronize()
+        out[name] = round(e0.elapsed_time(e1) / reps, 4)
+    return {"ms_per_op": out, "source": "reference Triton kernels compiled for sm_100 "
+                                        "(oracle/_ref), same inputs, CUDA events"}
 
 
 # ---------------------------------------------------------------- clocks
@@ -312,6 +498,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-device-baseline", action="store_true")
+    ap.add_argument("--no-tp-layer", action="store_true")
     ap.add_argument("--ncu-traffic", default=None,
                     help="ncu CSV (dram__bytes_read.sum, dram__bytes_write.sum) of this workload: "
                          "fills roofline.traffic with the attention kernels' DRAM bytes per call")
@@ -386,6 +574,14 @@ def main():
         e2e_ms = float(tt.item())
     e2e_val = step_bytes * ws / (e2e_ms / 1e3) / 1e9
 
+    # reference kernels on this GPU (one rank), then the tensor-parallel layer (all ranks)
+    dev_base = None
+    if rank == 0 and ws == 1 and not args.no_device_baseline:
+        dev_base = device_baseline(inp, dev)
+    del st
+    torch.cuda.empty_cache()
+    tp = run_tp_layer(ws, rank, dev) if not args.no_tp_layer else None
+
     peak, peak_kind = _peaks()
     attn_ms = statistics.median(per["attention"])
     achieved = nb["attention"] / (attn_ms / 1e3) / 1e9
@@ -417,6 +613,10 @@ def main():
                          "frac": round(achieved / peak, 4), "traffic": traffic,
                          "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)"},
             "cpu_baseline": cpu,
+            "device_baseline": None if dev_base is None else {
+                **dev_base, "speedup_per_op": {
+                    k: round(v / statistics.median(per[k]), 2) for k, v in dev_base["ms_per_op"].items()}},
+            "tp_layer": tp,
             "e2e": {"value": round(e2e_val, 3), "unit": "GB/s", "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h},
             "gpu_launches": 5 * args.steps,  # gemm, rms_norm, fxp_sum, 2 x attention

@@ -16,25 +16,32 @@ import torch
 import torch.distributed as dist
 
 
+def _pynccl():
+    from vllm.distributed import get_tp_group
+
+    tp = get_tp_group()
+    comm = getattr(tp, "device_communicator", None)
+    pynccl = getattr(comm, "pynccl_comm", None) if comm is not None else None
+    if pynccl is not None and getattr(pynccl, "disabled", True):
+        pynccl = None
+    return tp, pynccl
+
+
 def integer_all_reduce(t: torch.Tensor, group=None) -> torch.Tensor:
-    """Sum an int32/int64 tensor over a process group (exact). With
-    ``group=None`` the vLLM tensor-parallel group is used (its pynccl
-    communicator when available, which is CUDA-graph capturable)."""
+    """Sum an int32/int64 tensor over a process group (exact), in place when
+    possible. With ``group=None`` the vLLM tensor-parallel group is used (its
+    pynccl communicator when available, which is CUDA-graph capturable)."""
     if t.dtype not in (torch.int32, torch.int64):
         raise TypeError(f"integer_all_reduce expects int32/int64, got {t.dtype}")
     if group is not None:
         if dist.get_world_size(group) > 1:
             dist.all_reduce(t, op=dist.ReduceOp.SUM, group=group)
         return t
-    from vllm.distributed import get_tp_group
-
-    tp = get_tp_group()
+    tp, pynccl = _pynccl()
     if tp.world_size == 1:
         return t
-    comm = getattr(tp, "device_communicator", None)
-    pynccl = getattr(comm, "pynccl_comm", None) if comm is not None else None
-    if pynccl is not None and not getattr(pynccl, "disabled", True):
-        out = pynccl.all_reduce(t)
+    if pynccl is not None:
+        out = pynccl.all_reduce(t, t)
         if out is not None:
             return out
     dist.all_reduce(t, op=dist.ReduceOp.SUM, group=tp.device_group)
@@ -45,8 +52,21 @@ def integer_all_reduce(t: torch.Tensor, group=None) -> torch.Tensor:
 def integer_all_reduce_op(t: torch.Tensor) -> torch.Tensor:
     """Opaque op form of :func:`integer_all_reduce` over the vLLM TP group, so
     that torch.compile and CUDA-graph capture treat it as one node (vLLM's own
-    all-reduce op may route int tensors into float-only custom kernels)."""
-    return integer_all_reduce(t.clone())
+    all-reduce op may route int tensors into float-only custom kernels). The
+    op may not mutate its input: NCCL reduces out of place into a fresh
+    buffer (no copy of the input)."""
+    if t.dtype not in (torch.int32, torch.int64):
+        raise TypeError(f"integer_all_reduce expects int32/int64, got {t.dtype}")
+    tp, pynccl = _pynccl()
+    if tp.world_size == 1:
+        return t.clone()
+    if pynccl is not None:
+        out = pynccl.all_reduce(t, torch.empty_like(t))
+        if out is not None:
+            return out
+    out = t.clone()
+    dist.all_reduce(out, op=dist.ReduceOp.SUM, group=tp.device_group)
+    return out
 
 
 @integer_all_reduce_op.register_fake
