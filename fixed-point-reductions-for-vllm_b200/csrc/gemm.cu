@@ -69,6 +69,7 @@ struct Params {
   void* ws;       // int32/int64 partial tiles
   int* counters;  // per-tile tickets
   float one;      // 1.0f, opaque to the compiler (see the magic add below)
+  float2 cf2;     // (Cf, Cf), Cf = 1.5 * 2^(23 - frac): the scale-absorbing magic constant
 };
 
 template <int BITS> struct MinBlocks { static constexpr int v = 2; };
@@ -440,6 +441,280 @@ __global__ void __launch_bounds__(THREADS, MinBlocks<BITS>::v) gemm_kernel(Param
 }
 
 // ---------------------------------------------------------------------------
+// K-contiguous 16-bit operands (the linear-layer layout: activations [M, K],
+// weight [N, K] read as its transpose), the serving hot path.
+//
+// Both tiles are staged through registers (16-byte loads of chunk c+1 while
+// chunk c is computed) and converted once per CTA to fp32 in shared memory,
+// [rows][BK + 4] with k contiguous, so the inner loop reads k-pairs of both
+// operands with 16-byte loads (A: warp broadcast; B: four lanes a bank
+// group apart) and spends one packed FMA and one IADD3 per two products.
+//
+// The magic constant absorbs the 2^f scale: with Cf = 1.5 * 2^(23 - f), fp32
+// values in [2^(23 - f), 2^(24 - f)) are spaced 2^-f apart and Cf is an even
+// multiple of 2^-f, so RN(a * b + Cf) = Cf + RNE(a * b * 2^f) * 2^-f for an
+// exact product |a * b * 2^f| <= 2^22, and bits(r) - bits(Cf) is that
+// integer. No operand is scaled.
+// ---------------------------------------------------------------------------
+constexpr int KC_LD = BK + 4;  // fp32 row pitch of the staged tiles
+
+template <int BM, int BITS, typename T>
+__global__ void __launch_bounds__(THREADS, BM == 16 ? 4 : 2) gemm_kc_kernel(Params p) {
+  constexpr int TM = BM / 8;
+  constexpr int A_LOADS = BM * BK / 8 / THREADS;  // 16-byte loads of A per thread per chunk (BM 64: 1)
+  constexpr int A_THREADS = BM * BK / 8;          // threads that load A (BM 16: 64)
+  constexpr int B_LOADS = BN * BK / 8 / THREADS;  // 2
+  constexpr double LIMV = (BITS == 16) ? 32767.5 : 4194304.0;
+  static_assert(BK == 32 && BN == 128, "tile shape");
+
+  extern __shared__ __align__(16) unsigned char smem[];
+  float* As = reinterpret_cast<float*>(smem);                  // [2][BM][KC_LD]
+  float* Bs = As + 2 * BM * KC_LD;                             // [2][BN][KC_LD]
+  __shared__ uint32_t gmax[3][2];  // per chunk: max |a|, max |b| as fp32 patterns
+  __shared__ int s_last;
+
+  const int t = threadIdx.x, tx = t & 31, ty = t >> 5;
+  const int64_t tile = blockIdx.x;
+  const int split = blockIdx.y;
+  const int64_t m0 = (tile / p.tiles_n) * BM, n0 = (tile % p.tiles_n) * BN;
+  const int64_t nchunks = cdiv(p.K, BK);
+  const int64_t c0 = nchunks * split / p.splits, c1 = nchunks * (split + 1) / p.splits;
+  const int64_t nloc = c1 - c0;
+  const float scale = ldexpf(1.0f, p.frac);
+  const uint32_t cf_bits = __float_as_uint(p.cf2.x);
+  const T* A = reinterpret_cast<const T*>(p.a);
+  const T* B = reinterpret_cast<const T*>(p.b);
+  if (t < 6) (&gmax[0][0])[t] = 0u;
+
+  // this thread's 16-byte pieces: A row/k of load u, B column/k of load u
+  uint4 ra[A_LOADS > 0 ? A_LOADS : 1], rb[B_LOADS];
+  auto load_chunk = [&](int64_t c) {
+    const int64_t k0 = c * BK;
+#pragma unroll
+    for (int u = 0; u < (A_LOADS > 0 ? A_LOADS : 1); ++u) {
+      const int q = t + u * THREADS;
+      const int64_t m = m0 + q / (BK / 8), k = k0 + (q % (BK / 8)) * 8;
+      uint4 v = make_uint4(0, 0, 0, 0);
+      if (q < A_THREADS && m < p.M && k < p.K) v = *reinterpret_cast<const uint4*>(A + m * p.sam + k);
+      ra[u] = v;
+    }
+#pragma unroll
+    for (int u = 0; u < B_LOADS; ++u) {
+      const int q = t + u * THREADS;
+      const int64_t n = n0 + q / (BK / 8), k = k0 + (q % (BK / 8)) * 8;
+      uint4 v = make_uint4(0, 0, 0, 0);
+      if (n < p.N && k < p.K) v = __ldcs(reinterpret_cast<const uint4*>(B + n * p.sbn + k));
+      rb[u] = v;
+    }
+  };
+  // convert the staged pieces into buffer `buf` and fold their |x| into gmax[slot]
+  auto store_chunk = [&](int buf, int slot) {
+    uint32_t mu_a = 0, ms_a = 0x80008000u, mu_b = 0, ms_b = 0x80008000u;
+    float* Ad = As + buf * BM * KC_LD;
+    float* Bd = Bs + buf * BN * KC_LD;
+    auto put = [&](float* dst, uint4 v) {
+      const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+      float f[8];
+#pragma unroll
+      for (int h = 0; h < 4; ++h) {
+        if constexpr (std::is_same<T, __nv_bfloat16>::value) {
+          f[2 * h] = __uint_as_float(w[h] << 16);
+          f[2 * h + 1] = __uint_as_float(w[h] & 0xFFFF0000u);
+        } else {
+          const float2 g = __half22float2(*reinterpret_cast<const __half2*>(&w[h]));
+          f[2 * h] = g.x;
+          f[2 * h + 1] = g.y;
+        }
+      }
+      *reinterpret_cast<float4*>(dst) = make_float4(f[0], f[1], f[2], f[3]);
+      *reinterpret_cast<float4*>(dst + 4) = make_float4(f[4], f[5], f[6], f[7]);
+    };
+#pragma unroll
+    for (int u = 0; u < (A_LOADS > 0 ? A_LOADS : 1); ++u) {
+      const int q = t + u * THREADS;
+      if (q < A_THREADS) {
+        put(Ad + (q / (BK / 8)) * KC_LD + (q % (BK / 8)) * 8, ra[u]);
+        mu_a = __vimax3_u16x2(mu_a, ra[u].x, ra[u].y);
+        mu_a = __vimax3_u16x2(mu_a, ra[u].z, ra[u].w);
+        ms_a = (uint32_t)__vimax3_s16x2((int)ms_a, (int)ra[u].x, (int)ra[u].y);
+        ms_a = (uint32_t)__vimax3_s16x2((int)ms_a, (int)ra[u].z, (int)ra[u].w);
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < B_LOADS; ++u) {
+      const int q = t + u * THREADS;
+      put(Bd + (q / (BK / 8)) * KC_LD + (q % (BK / 8)) * 8, rb[u]);
+      mu_b = __vimax3_u16x2(mu_b, rb[u].x, rb[u].y);
+      mu_b = __vimax3_u16x2(mu_b, rb[u].z, rb[u].w);
+      ms_b = (uint32_t)__vimax3_s16x2((int)ms_b, (int)rb[u].x, (int)rb[u].y);
+      ms_b = (uint32_t)__vimax3_s16x2((int)ms_b, (int)rb[u].z, (int)rb[u].w);
+    }
+    // |x| bounds as fp32 patterns (16-bit halves -> max magnitude -> fp32)
+    auto bound = [](uint32_t mu, uint32_t ms) -> uint32_t {
+      const uint32_t pk = __vmaxu2(mu & 0x7FFF7FFFu, ms & 0x7FFF7FFFu);
+      return abs_max_as_f32<T>(max(pk & 0xFFFFu, pk >> 16));
+    };
+    const uint32_t ba = __reduce_max_sync(0xffffffffu, bound(mu_a, ms_a));
+    const uint32_t bb = __reduce_max_sync(0xffffffffu, bound(mu_b, ms_b));
+    if (tx == 0) {
+      atomicMax(&gmax[slot][0], ba);
+      atomicMax(&gmax[slot][1], bb);
+    }
+  };
+
+  uint32_t acc[TM][TN];
+  unsigned long long acc64[TM][TN];
+#pragma unroll
+  for (int i = 0; i < TM; ++i)
+#pragma unroll
+    for (int j = 0; j < TN; ++j) {
+      acc[i][j] = 0u;
+      acc64[i][j] = 0ull;
+    }
+
+  if (nloc > 0) load_chunk(c0);
+  __syncthreads();  // gmax zeroed
+  if (nloc > 0) store_chunk(0, 0);
+  if (nloc > 1) load_chunk(c0 + 1);
+  __syncthreads();
+
+  const float2 CF2 = p.cf2;  // a kernel parameter: the packed FMA reads it from the constant bank
+  for (int64_t it = 0; it < nloc; ++it) {
+    const int buf = (int)(it & 1), slot = (int)(it % 3);
+    const float ma = __uint_as_float(gmax[slot][0]), mb = __uint_as_float(gmax[slot][1]);
+    // fast iff max|a| * max|b| * 2^f < 2^22 (int16: < 32767.5); NaN/inf fail
+    const bool fast = (double)__fmul_ru(ma, mb) * (double)scale < LIMV;
+    if (t == 0) {  // the slot read two chunks ago is free again
+      const int z = (int)((it + 2) % 3);
+      gmax[z][0] = 0u;
+      gmax[z][1] = 0u;
+    }
+    const float* Ab = As + buf * BM * KC_LD + (ty * TM) * KC_LD;
+    const float* Bb = Bs + buf * BN * KC_LD + tx * KC_LD;
+    if (fast) {
+#pragma unroll
+      for (int kk = 0; kk < BK; kk += 4) {
+        float4 bv[TN];
+#pragma unroll
+        for (int j = 0; j < TN; ++j) bv[j] = *reinterpret_cast<const float4*>(Bb + j * 32 * KC_LD + kk);
+#pragma unroll
+        for (int i = 0; i < TM; ++i) {
+          const float4 av = *reinterpret_cast<const float4*>(Ab + i * KC_LD + kk);
+          const float2 a0 = make_float2(av.x, av.y), a1 = make_float2(av.z, av.w);
+#pragma unroll
+          for (int j = 0; j < TN; ++j) {
+            const float2 r0 = fma2(a0, make_float2(bv[j].x, bv[j].y), CF2);
+            const float2 r1 = fma2(a1, make_float2(bv[j].z, bv[j].w), CF2);
+            acc[i][j] += __float_as_uint(r0.x) + __float_as_uint(r0.y);
+            acc[i][j] += __float_as_uint(r1.x) + __float_as_uint(r1.y);
+          }
+        }
+      }
+#pragma unroll
+      for (int i = 0; i < TM; ++i)
+#pragma unroll
+        for (int j = 0; j < TN; ++j) {
+          acc[i][j] -= (uint32_t)BK * cf_bits;
+          if constexpr (BITS == 64) {
+            acc64[i][j] += (unsigned long long)(long long)(int32_t)acc[i][j];
+            acc[i][j] = 0u;
+          }
+        }
+    } else {
+      // exact reference path on the staged (exact) fp32 values
+#pragma unroll 1
+      for (int kk = 0; kk < BK; ++kk) {
+#pragma unroll
+        for (int i = 0; i < TM; ++i) {
+          const float a = Ab[i * KC_LD + kk];
+#pragma unroll
+          for (int j = 0; j < TN; ++j) {
+            const auto v = f2x_f32<BITS>(__fmul_rn(a, Bb[j * 32 * KC_LD + kk]), scale);
+            if constexpr (BITS == 64) {
+              acc64[i][j] += (unsigned long long)v;
+            } else {
+              acc[i][j] += (uint32_t)v;
+            }
+          }
+        }
+      }
+    }
+    if (it + 1 < nloc) store_chunk(buf ^ 1, (int)((it + 1) % 3));
+    if (it + 2 < nloc) load_chunk(c0 + it + 2);
+    __syncthreads();
+  }
+
+  // ---- epilogue (as gemm_kernel: direct store, or split-K integer atomics) ----
+  const float inv = ldexpf(1.0f, -p.frac);
+  auto final_store = [&](int64_t m, int64_t n, unsigned long long v) {
+    if (p.out_kind == 0) {
+      float f;
+      if constexpr (BITS == 64) {
+        f = x2f_f32<64>((long long)v, inv);
+      } else {
+        f = x2f_f32<BITS>(wrap_acc<BITS>((int32_t)(uint32_t)v), inv);
+      }
+      reinterpret_cast<float*>(p.c)[m * p.scm + n * p.scn] = f;
+    } else if constexpr (BITS == 64) {
+      reinterpret_cast<long long*>(p.c)[m * p.scm + n * p.scn] = (long long)v;
+    } else {
+      reinterpret_cast<int32_t*>(p.c)[m * p.scm + n * p.scn] = (int32_t)(uint32_t)v;
+    }
+  };
+  auto value = [&](int i, int j) -> unsigned long long {
+    if constexpr (BITS == 64) return acc64[i][j];
+    else return (unsigned long long)acc[i][j];
+  };
+  if (p.splits == 1) {
+#pragma unroll
+    for (int i = 0; i < TM; ++i)
+#pragma unroll
+      for (int j = 0; j < TN; ++j) {
+        const int64_t m = m0 + ty * TM + i, n = n0 + tx + 32 * j;
+        if (m < p.M && n < p.N) final_store(m, n, value(i, j));
+      }
+    return;
+  }
+  const int64_t wbase = tile * (int64_t)BM * BN;
+#pragma unroll
+  for (int i = 0; i < TM; ++i)
+#pragma unroll
+    for (int j = 0; j < TN; ++j) {
+      const int ml = ty * TM + i, nl = tx + 32 * j;
+      if (m0 + ml < p.M && n0 + nl < p.N) {
+        if constexpr (BITS == 64) {
+          atomicAdd(reinterpret_cast<unsigned long long*>(p.ws) + wbase + ml * BN + nl, acc64[i][j]);
+        } else {
+          atomicAdd(reinterpret_cast<unsigned int*>(p.ws) + wbase + ml * BN + nl, acc[i][j]);
+        }
+      }
+    }
+  __threadfence();
+  __syncthreads();
+  if (t == 0) s_last = (atomicAdd(p.counters + tile, 1) == p.splits - 1);
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();
+#pragma unroll
+  for (int i = 0; i < TM; ++i)
+#pragma unroll
+    for (int j = 0; j < TN; ++j) {
+      const int ml = ty * TM + i, nl = tx + 32 * j;
+      const int64_t m = m0 + ml, n = n0 + nl;
+      if (m < p.M && n < p.N) {
+        unsigned long long v;
+        if constexpr (BITS == 64) {
+          v = atomicExch(reinterpret_cast<unsigned long long*>(p.ws) + wbase + ml * BN + nl, 0ull);
+        } else {
+          v = atomicExch(reinterpret_cast<unsigned int*>(p.ws) + wbase + ml * BN + nl, 0u);
+        }
+        final_store(m, n, v);
+      }
+    }
+  if (t == 0) p.counters[tile] = 0;
+}
+
+// ---------------------------------------------------------------------------
 // host side
 // ---------------------------------------------------------------------------
 struct Plan {
@@ -448,12 +723,15 @@ struct Plan {
   int splits;
 };
 
-static Plan make_plan(int64_t M, int64_t N, int64_t K) {
+// Tile height: 16 rows for M <= 16, 32 for M <= 32 (and with 64-bit
+// accumulators, whose extra int64 registers would not fit 64 rows), else 64
+static Plan make_plan(int64_t M, int64_t N, int64_t K, int bits) {
   Plan pl;
-  pl.bm = M <= 16 ? 16 : 64;
+  pl.bm = M <= 16 ? 16 : ((M <= 32 || bits == 64) ? 32 : 64);
   pl.tiles_n = cdiv(N, BN);
   pl.tiles = cdiv(M, pl.bm) * pl.tiles_n;
-  const int64_t target = (int64_t)num_sms() * 2;  // two resident CTAs per SM
+  // resident CTAs per SM: 16-row tiles are small enough for four
+  const int64_t target = (int64_t)num_sms() * (pl.bm == 16 ? 4 : 2);
   const int64_t nchunks = cdiv(K, BK);
   int64_t s = pl.tiles >= target ? 1 : target / pl.tiles;
   const int64_t smax = nchunks / 2 > 1 ? nchunks / 2 : 1;  // >= 2 chunks per split
@@ -504,8 +782,39 @@ static int pick_layout(const Params& p, int64_t tiles, bool exact, cudaStream_t 
   return launch<BM, BITS, BT, B_GENERIC, false>(p, tiles, st);
 }
 
+template <int BM, int BITS, typename T>
+static int launch_kc(const Params& p, int64_t tiles, cudaStream_t st) {
+  auto k = gemm_kc_kernel<BM, BITS, T>;
+  const int smem = 2 * (BM + BN) * KC_LD * (int)sizeof(float);
+  static bool configured[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64 || !configured[dev]) {
+    if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess) {
+      set_error("gemm_fxp: cannot configure %d bytes of shared memory", smem);
+      return FXPR_ERR_CUDA;
+    }
+    if (dev >= 0 && dev < 64) configured[dev] = true;
+  }
+  const dim3 grid((unsigned)tiles, (unsigned)p.splits);
+  k<<<grid, THREADS, smem, st>>>(p);
+  return check_launch("fxpr_gemm_fxp");
+}
+
+// both operands 16-bit of one type, k contiguous, 16-byte aligned rows
+static bool kc_ok(const Params& p, int b_dtype) {
+  if (p.a_dtype != b_dtype || (b_dtype != FXPR_BF16 && b_dtype != FXPR_F16)) return false;
+  if (p.sak != 1 || p.sbk != 1 || p.K % 8 != 0) return false;
+  if ((uintptr_t)p.a % 16 != 0 || (uintptr_t)p.b % 16 != 0) return false;
+  if (p.sam % 8 != 0 || p.sbn % 8 != 0) return false;
+  return p.frac >= 0 && p.frac <= 100;
+}
+
 template <int BM, int BITS>
 static int pick_btype(const Params& p, int b_dtype, int64_t tiles, cudaStream_t st) {
+  if (kc_ok(p, b_dtype))
+    return b_dtype == FXPR_BF16 ? launch_kc<BM, BITS, __nv_bfloat16>(p, tiles, st)
+                                : launch_kc<BM, BITS, __half>(p, tiles, st);
   const bool a16 = p.a_dtype == FXPR_BF16 || p.a_dtype == FXPR_F16;
   switch (b_dtype) {
     case FXPR_BF16: return pick_layout<BM, BITS, __nv_bfloat16>(p, tiles, a16, st);
@@ -521,7 +830,7 @@ using namespace fxpr;
 
 extern "C" int64_t fxpr_gemm_workspace_bytes(int64_t M, int64_t N, int64_t K, int int_bits) {
   if (M <= 0 || N <= 0) return 0;
-  return gemm::ws_bytes(gemm::make_plan(M, N, K), int_bits);
+  return gemm::ws_bytes(gemm::make_plan(M, N, K, int_bits), int_bits);
 }
 
 extern "C" int fxpr_gemm_fxp(const void* a, int a_dtype, int64_t sam, int64_t sak, const void* b,
@@ -551,7 +860,7 @@ extern "C" int fxpr_gemm_fxp(const void* a, int a_dtype, int64_t sam, int64_t sa
     return FXPR_ERR_INVALID;
   }
   if (M == 0 || N == 0) return FXPR_OK;
-  const gemm::Plan pl = gemm::make_plan(M, N, K);
+  const gemm::Plan pl = gemm::make_plan(M, N, K, int_bits);
   if (pl.tiles > 0x7fffffffLL) {
     set_error("gemm_fxp: problem too large");
     return FXPR_ERR_INVALID;
@@ -566,6 +875,7 @@ extern "C" int fxpr_gemm_fxp(const void* a, int a_dtype, int64_t sam, int64_t sa
   p.b = b; p.sbk = sbk; p.sbn = sbn;
   p.c = c; p.out_kind = out_kind; p.scm = scm; p.scn = scn;
   p.M = M; p.N = N; p.K = K; p.frac = frac_bits; p.one = 1.0f;
+  p.cf2 = make_float2(ldexpf(1.5f, 23 - frac_bits), ldexpf(1.5f, 23 - frac_bits));
   p.splits = pl.splits; p.tiles_n = pl.tiles_n;
   p.ws = workspace;
   p.counters = need > 0 ? reinterpret_cast<int*>(reinterpret_cast<char*>(workspace) + need -
@@ -577,9 +887,13 @@ extern "C" int fxpr_gemm_fxp(const void* a, int a_dtype, int64_t sam, int64_t sa
     if (int_bits == 32) return gemm::pick_btype<16, 32>(p, b_dtype, pl.tiles, st);
     return gemm::pick_btype<16, 64>(p, b_dtype, pl.tiles, st);
   }
+  if (pl.bm == 32) {
+    if (int_bits == 16) return gemm::pick_btype<32, 16>(p, b_dtype, pl.tiles, st);
+    if (int_bits == 32) return gemm::pick_btype<32, 32>(p, b_dtype, pl.tiles, st);
+    return gemm::pick_btype<32, 64>(p, b_dtype, pl.tiles, st);
+  }
   if (int_bits == 16) return gemm::pick_btype<64, 16>(p, b_dtype, pl.tiles, st);
-  if (int_bits == 32) return gemm::pick_btype<64, 32>(p, b_dtype, pl.tiles, st);
-  return gemm::pick_btype<64, 64>(p, b_dtype, pl.tiles, st);
+  return gemm::pick_btype<64, 32>(p, b_dtype, pl.tiles, st);
 }
 
 // ---------------------------------------------------------------------------

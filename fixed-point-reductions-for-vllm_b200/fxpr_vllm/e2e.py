@@ -28,7 +28,7 @@ PRESETS = {
                     rms_norm_eps=1e-5, rope_theta=500000.0, vocab_size=128256),
     # tiny model for tests
     "tiny": dict(hidden_size=256, num_hidden_layers=2, num_attention_heads=8,
-                 num_key_value_heads=2, head_dim=32, intermediate_size=512,
+                 num_key_value_heads=2, head_dim=64, intermediate_size=512,
                  rms_norm_eps=1e-5, rope_theta=500000.0, vocab_size=1024),
 }
 

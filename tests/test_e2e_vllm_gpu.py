@@ -44,6 +44,8 @@ def test_greedy_streams_identical_and_fixed_point_kernels_used(tmp_path):
     assert a["full"] == a["one"] == a["three"]
     assert all(len(s) == 24 for s in a["full"])
     ks = " ".join(a["kernels"])
-    # GEMM, RMSNorm (row or vector variant) and the chunked attention kernels
-    for k in ("gemm_kernel", "rms_norm", "chunk_scores", "chunk_pv_kernel"):
+    # the fixed-point GEMM, RMSNorm, prefill attention (chunked kernels) and
+    # decode attention (persistent decode kernels)
+    for k in ("gemm_kc_kernel", "rms_norm", "chunk_scores", "chunk_pv_kernel", "dq_scores_kernel",
+              "dq_pv_kernel"):
         assert k in ks, (k, a["kernels"])
