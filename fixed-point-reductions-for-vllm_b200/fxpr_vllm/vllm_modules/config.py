@@ -10,6 +10,8 @@ Environment variables, read once into a frozen process-wide config:
 ``VLLM_FXP_DET_GEMM``           on       fixed_point_det linear method
 ``VLLM_FXP_DET_ATTN``           on       CUSTOM attention backend
 ``VLLM_FXP_DET_LOGPROBS``       on       deterministic sampler log-softmax
+``VLLM_FXP_DET_LM_HEAD``        on       fixed-point LM-head logits GEMM (an addition:
+                                         the reference's LM head is a float GEMM)
 =============================  =======  ==========================================
 
 A malformed or out-of-range value logs a warning and falls back to the
@@ -65,6 +67,7 @@ _SWITCHES = {
     "enable_gemm": "VLLM_FXP_DET_GEMM",
     "enable_attn": "VLLM_FXP_DET_ATTN",
     "enable_logprobs": "VLLM_FXP_DET_LOGPROBS",
+    "enable_lm_head": "VLLM_FXP_DET_LM_HEAD",
 }
 _OFF_WORDS = frozenset({"0", "false", "no", "off"})
 
@@ -78,6 +81,7 @@ class FxpRuntimeConfig:
     enable_gemm: bool = True
     enable_attn: bool = True
     enable_logprobs: bool = True
+    enable_lm_head: bool = True
 
 
 def _resolve_int(knob: _IntKnob, env: Mapping[str, str], got: Mapping[str, object]) -> int:

@@ -9,6 +9,13 @@ Differences from the reference that do not change results:
   (``tp_allreduce.integer_all_reduce``) before X2F + bias, with the bias added
   on every rank after the reduce, so outputs are identical for every TP degree
   (the reference float-allreduces after X2F, which is not TP-invariant).
+
+Addition (not in the reference, whose ``get_quant_method`` returns ``None``
+for the LM head, quantisation_config.py:91-93): with ``VLLM_FXP_DET_LM_HEAD``
+on (the default) the ``ParallelLMHead`` logits GEMM is fixed-point too
+(:class:`FixedPointLMHeadMethod`), so no float reduction is left between the
+last hidden state and the greedy argmax. Vocab-parallel shards are gathered,
+not summed, so the logits stay independent of the TP degree.
 """
 
 from __future__ import annotations
@@ -20,6 +27,10 @@ from typing import Any
 import torch
 import torch.nn as nn
 from vllm.model_executor.layers.linear import LinearBase, RowParallelLinear
+from vllm.model_executor.layers.vocab_parallel_embedding import (
+    ParallelLMHead,
+    UnquantizedEmbeddingMethod,
+)
 from vllm.model_executor.layers.quantization import register_quantization_config
 from vllm.model_executor.layers.quantization.base_config import (
     QuantizationConfig,
@@ -70,6 +81,8 @@ class FixedPointConfig(QuantizationConfig):
     def get_quant_method(self, layer: nn.Module, prefix: str) -> "QuantizeMethodBase | None":
         if isinstance(layer, LinearBase):
             return FixedPointLinearMethod(self)
+        if isinstance(layer, ParallelLMHead) and get_runtime_config().enable_lm_head:
+            return FixedPointLMHeadMethod(self)
         return None
 
     def get_scaled_act_names(self) -> list[str]:
@@ -127,4 +140,31 @@ class FixedPointLinearMethod(QuantizeMethodBase):
                 bias = layer.bias
         out = torch.ops.fxpr.fixed_to_float_bias(acc, bias, self.config.frac_bits,
                                                  self.fxp_int_bits, orig_dtype)
+        return out.view(*x.shape[:-1], out.shape[-1])
+
+
+class FixedPointLMHeadMethod(UnquantizedEmbeddingMethod):
+    """Logits of a ``ParallelLMHead`` through the fixed-point GEMM: the weight
+    stays the bf16 ``[vocab_shard, hidden]`` parameter (possibly tied to the
+    input embedding, whose lookup is unchanged), ``x`` is cast to the weight
+    dtype, and each rank computes its vocabulary shard as
+    ``cast(X2F(sum_k F2X(x * w)) + bias)``, like FixedPointLinearMethod.apply."""
+
+    def __init__(self, config: FixedPointConfig) -> None:
+        super().__init__()
+        self.config = config
+        self.fxp_int_bits = get_runtime_config().fxp_int_bits
+
+    def apply(self, layer: nn.Module, x: torch.Tensor, bias: torch.Tensor | None = None) -> torch.Tensor:
+        w = layer.weight
+        if w.dtype != torch.bfloat16:
+            w = w.to(torch.bfloat16)
+        x2d = x.reshape(-1, x.shape[-1])
+        if x2d.dtype != w.dtype:
+            x2d = x2d.to(w.dtype)
+        if not x2d.is_contiguous():
+            x2d = x2d.contiguous()
+        acc = torch.ops.fxpr.gemm_fxp_int(x2d, w.t(), self.config.frac_bits, self.fxp_int_bits)
+        out = torch.ops.fxpr.fixed_to_float_bias(acc, bias, self.config.frac_bits, self.fxp_int_bits,
+                                                 x.dtype)
         return out.view(*x.shape[:-1], out.shape[-1])

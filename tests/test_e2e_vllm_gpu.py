@@ -49,3 +49,5 @@ def test_greedy_streams_identical_and_fixed_point_kernels_used(tmp_path):
     for k in ("gemm_kc_kernel", "rms_norm", "chunk_scores", "chunk_pv_kernel", "dq_scores_kernel",
               "dq_pv_kernel"):
         assert k in ks, (k, a["kernels"])
+    # no float GEMM left: the LM head runs the fixed-point GEMM too
+    assert not any("nvjet" in k or "cublas" in k.lower() for k in a["kernels"]), a["kernels"]

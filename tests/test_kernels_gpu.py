@@ -266,3 +266,20 @@ def test_linear_method_apply_matches_oracle():
     layer = SimpleNamespace(weight_t=wd.t(), fxp_weight=wd, bias=None, fxp_int_reduce=False)
     got = m.apply(layer, x.cuda(), bias.cuda()).cpu()
     assert bits_equal(got, O.linear_apply(x, w, bias, 16, m.fxp_int_bits))
+
+
+def test_lm_head_method_matches_oracle():
+    """FixedPointLMHeadMethod.apply: logits of a vocabulary shard through the
+    fixed-point GEMM, bf16 hidden states, with and without a bias."""
+    from types import SimpleNamespace
+
+    from fxpr_vllm.vllm_modules.quantisation_config import FixedPointConfig, FixedPointLMHeadMethod
+
+    g = torch.Generator().manual_seed(9)
+    x = torch.randn(5, 1024, generator=g).to(torch.bfloat16)
+    w = (torch.randn(3000, 1024, generator=g) * 0.02).to(torch.bfloat16)
+    m = FixedPointLMHeadMethod(FixedPointConfig(16))
+    layer = SimpleNamespace(weight=w.cuda())
+    for bias in (None, torch.randn(3000, generator=g).to(torch.bfloat16)):
+        got = m.apply(layer, x.cuda(), None if bias is None else bias.cuda()).cpu()
+        assert bits_equal(got, O.linear_apply(x, w, bias, 16, m.fxp_int_bits))

@@ -74,3 +74,24 @@ def test_fixed_point_config_api():
 
     assert cfg.get_quant_method(nn.Linear(2, 2), "x") is None
     assert isinstance(FixedPointLinearMethod(cfg), FixedPointLinearMethod)
+
+
+def test_lm_head_routed_to_fixed_point(monkeypatch):
+    """The LM head gets the fixed-point logits method (an addition to the
+    reference, gated by VLLM_FXP_DET_LM_HEAD); embeddings keep vLLM's own."""
+    from fxpr_vllm.vllm_modules import config as C
+    from fxpr_vllm.vllm_modules.quantisation_config import FixedPointConfig, FixedPointLMHeadMethod
+    from vllm.model_executor.layers.vocab_parallel_embedding import ParallelLMHead, VocabParallelEmbedding
+
+    head = ParallelLMHead.__new__(ParallelLMHead)
+    emb = VocabParallelEmbedding.__new__(VocabParallelEmbedding)
+    old = C._runtime_config
+    try:
+        C._runtime_config = C.FxpRuntimeConfig()
+        cfg = FixedPointConfig(16)
+        assert isinstance(cfg.get_quant_method(head, "lm_head"), FixedPointLMHeadMethod)
+        assert cfg.get_quant_method(emb, "embed_tokens") is None
+        C._runtime_config = C.FxpRuntimeConfig(enable_lm_head=False)
+        assert cfg.get_quant_method(head, "lm_head") is None
+    finally:
+        C._runtime_config = old
