@@ -246,9 +246,9 @@ class TPLayer:
         A.unified_attention_fxp(q, self.kv, self.o, self.qsl, self.seq_lens, self.bt, 1, fxp_dtype=B,
                                 frac_bits=F, max_seq_len=self.CTX)
         part = op.gemm_fxp_int(self.o.view(self.TOK, -1), self.w_o.t(), F, B)
-        attn_out = op.fixed_to_float_bias(self._allreduce(part, ev[0] if ev else None), None, F, B,
-                                          torch.bfloat16)
-        h2 = op.rms_norm_fxp_residual(attn_out, res, self.norm2, 1e-5, F, B)
+        # X2F of the reduced partials, residual add and RMSNorm in one kernel
+        h2 = op.fixed_to_float_add_rms_norm(self._allreduce(part, ev[0] if ev else None), None, res,
+                                            self.norm2, 1e-5, F, B)
         gu = op.fixed_to_float_bias(op.gemm_fxp_int(h2, self.w_gu.t(), F, B), None, F, B, torch.bfloat16)
         f = gu.shape[1] // 2
         act = torch.nn.functional.silu(gu[:, :f]) * gu[:, f:]

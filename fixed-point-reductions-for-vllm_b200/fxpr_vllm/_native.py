@@ -34,7 +34,7 @@ EXPORTED = (
     "fxpr_abi_version", "fxpr_last_error", "fxpr_float_to_fixed", "fxpr_fixed_to_float",
     "fxpr_fxp_sum", "fxpr_gemm_workspace_bytes", "fxpr_gemm_fxp", "fxpr_fixed_to_float_bias",
     "fxpr_rms_norm_fxp", "fxpr_unified_attention_fxp", "fxpr_log_softmax_fxp", "fxpr_probe_prims",
-    "fxpr_gemm_fxp_noalloc", "fxpr_attention_workspace_bytes",
+    "fxpr_gemm_fxp_noalloc", "fxpr_attention_workspace_bytes", "fxpr_fixed_to_float_add_rms_norm",
 )
 
 _i = ctypes.c_int
@@ -81,6 +81,8 @@ _SIGS = {
     "fxpr_fixed_to_float_bias": (_i, [_p, _i, _i64, _i64, _i64, _p, _i, _p, _i, _i64, _i, _p]),
     "fxpr_rms_norm_fxp": (_i, [_p, _i, _i64, _p, _i, _p, _i, _i64, _p, _i, _i64, _i64, _i64,
                                _f, _i, _i, _p]),
+    "fxpr_fixed_to_float_add_rms_norm": (_i, [_p, _i, _i64, _p, _i, _p, _i, _i64, _p, _i, _p, _i64,
+                                              _i64, _i64, _f, _i, _p]),
     "fxpr_unified_attention_fxp": (_i, [ctypes.POINTER(AttentionParams), _p]),
     "fxpr_attention_workspace_bytes": (_i64, [ctypes.POINTER(AttentionParams)]),
     "fxpr_log_softmax_fxp": (_i, [_p, _i64, _p, _i64, _i64, _i64, _i, _i, _p]),

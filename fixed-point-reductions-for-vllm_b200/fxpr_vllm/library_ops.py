@@ -140,3 +140,16 @@ def log_softmax_fxp(x: torch.Tensor, fxp_int_bits: int, dim: int, frac_bits: int
 @log_softmax_fxp.register_fake
 def _(x, fxp_int_bits, dim, frac_bits):
     return torch.empty_like(x)
+
+
+@torch.library.custom_op("fxpr::fixed_to_float_add_rms_norm", mutates_args=("residual",),
+                         device_types="cuda")
+def fixed_to_float_add_rms_norm(acc: torch.Tensor, bias: torch.Tensor | None, residual: torch.Tensor,
+                                weight: torch.Tensor, eps: float, frac_bits: int,
+                                fxp_int_bits: int) -> torch.Tensor:
+    return _rms.fixed_to_float_add_rms_norm(acc, bias, residual, weight, eps, frac_bits, fxp_int_bits)
+
+
+@fixed_to_float_add_rms_norm.register_fake
+def _(acc, bias, residual, weight, eps, frac_bits, fxp_int_bits):
+    return torch.empty_like(residual)

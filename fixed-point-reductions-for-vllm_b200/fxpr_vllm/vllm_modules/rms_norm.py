@@ -30,11 +30,12 @@ class DeterministicRMSNorm(RMSNorm):
         if not x.is_cuda:
             raise RuntimeError("DeterministicRMSNorm requires CUDA tensors (no CPU implementation)")
         if residual is not None:
-            new_residual = residual.clone()  # the caller's residual is not mutated
+            # residual += x in place, as vLLM's own fused add + RMSNorm does
+            # (the reference returns an updated copy; callers use the returned one)
             out = torch.ops.fxpr.rms_norm_fxp_residual(
-                x, new_residual, self.weight, self.variance_epsilon, self._fxp_frac_bits,
+                x, residual, self.weight, self.variance_epsilon, self._fxp_frac_bits,
                 self._fxp_int_bits)
-            return out, new_residual
+            return out, residual
         return torch.ops.fxpr.rms_norm_fxp(x, self.weight, self.variance_epsilon,
                                            self._fxp_frac_bits, self._fxp_int_bits)
 

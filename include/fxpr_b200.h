@@ -112,6 +112,20 @@ int fxpr_rms_norm_fxp(const void* x, int x_dtype, int64_t x_row_stride, const vo
                       int res_dtype, int64_t res_row_stride, int64_t rows, int64_t hidden,
                       float eps, int frac_bits, int int_bits, void* stream);
 
+/* Row-parallel linear epilogue fused with the residual RMSNorm: per row,
+ * h = cast_act(X2F(acc) + fp32(bias)) (the linear layer's output, acc int32
+ * for int_bits 16/32 -- low 16 bits for 16 -- or int64), v = fp32(h) +
+ * fp32(residual) written back to residual in act_dtype, y = fixed-point
+ * RMSNorm of v (as fxpr_rms_norm_fxp) in act_dtype. bias may be NULL.
+ * Replaces the pair quantisation_config.py:181-187 (fixed_to_float + bias +
+ * cast after the allreduce) and library_ops.py:88-126
+ * (fxpr::rms_norm_fxp_residual) with one pass; same bits. */
+int fxpr_fixed_to_float_add_rms_norm(const void* acc, int int_bits, int64_t acc_row_stride,
+                                     const void* bias, int bias_dtype, void* residual, int act_dtype,
+                                     int64_t res_row_stride, const void* w, int w_dtype, void* y,
+                                     int64_t y_row_stride, int64_t rows, int64_t hidden, float eps,
+                                     int frac_bits, void* stream);
+
 /* Paged unified (prefill + decode) attention with fixed-point softmax
  * normaliser and PV accumulation and a bit-exact integer split-KV combine.
  * Replaces fixed_point_kernels/attention.py:398-489 (unified_attention_fxp)

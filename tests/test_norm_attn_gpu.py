@@ -291,3 +291,38 @@ def test_attention_understated_hint(monkeypatch, prims):
     torch.cuda.synchronize()
     exp = _oracle_attn(q[:1], kv, qsl[:2], sl[:1], bt[:1], 1, prims, frac_bits=16)
     assert bits_equal(o[:1].cpu(), exp)
+
+
+@pytest.mark.parametrize("bits", [16, 32, 64])
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+def test_fixed_to_float_add_rms_norm(prims, bits, dtype):
+    """The fused row-parallel epilogue + residual RMSNorm against the oracle
+    composition (linear epilogue, quantisation_config.py:181-187, then
+    rms_norm.py:36-59) and against the two unfused device ops."""
+    from fxpr_vllm import library_ops  # noqa: F401
+
+    g = torch.Generator().manual_seed(bits)
+    f = 8 if bits == 16 else 16
+    for rows, hidden in [(3, 4096), (7, 1000)]:
+        lim = 2 ** (15 if bits == 16 else 30)
+        acc = torch.randint(-lim, lim, (rows, hidden), generator=g,
+                            dtype=torch.int64 if bits == 64 else torch.int32)
+        bias = torch.randn(hidden, generator=g).to(dtype)
+        res = torch.randn(rows, hidden, generator=g).to(dtype)
+        w = (1 + 0.1 * torch.randn(hidden, generator=g)).to(dtype)
+        for b in (None, bias):
+            rd = res.clone().cuda()
+            y = torch.ops.fxpr.fixed_to_float_add_rms_norm(acc.cuda(), None if b is None else b.cuda(), rd,
+                                                           w.cuda(), 1e-5, f, bits)
+            # oracle: X2F + bias in fp32, cast to the activation dtype, residual RMSNorm
+            a = acc if bits != 16 else O.wrap_int(acc.to(torch.int64), 16)
+            h = O.fixed_to_float(a, f, torch.float32)
+            if b is not None:
+                h = h + b.to(torch.float32)
+            ey, er = O.rms_norm_fxp(h.to(dtype), w, 1e-5, f, bits, residual=res, prims=prims)
+            assert bits_equal(y.cpu(), ey) and bits_equal(rd.cpu(), er), (rows, hidden, b is None)
+            # the unfused pair on the device
+            r2 = res.clone().cuda()
+            h2 = torch.ops.fxpr.fixed_to_float_bias(acc.cuda(), None if b is None else b.cuda(), f, bits, dtype)
+            y2 = torch.ops.fxpr.rms_norm_fxp_residual(h2, r2, w.cuda(), 1e-5, f, bits)
+            assert bits_equal(y, y2) and bits_equal(rd, r2)
