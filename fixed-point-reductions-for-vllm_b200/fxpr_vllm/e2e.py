@@ -126,6 +126,51 @@ def _timed(fn, *a):
     return time.perf_counter() - t0
 
 
+def streams_sha(streams) -> str:
+    import hashlib
+
+    return hashlib.sha256(json.dumps(streams).encode()).hexdigest()[:16]
+
+
+def _tp_list(args) -> None:
+    """Run one fresh process per TP degree of ``--tp-list`` (vLLM engines do
+    not release their GPUs within a process), collect decode tok/s and the
+    greedy streams of each, and report whether every degree produced the
+    same streams (and the same as ``--ref-streams`` when given)."""
+    import subprocess
+    import tempfile
+
+    rows, streams = [], {}
+    ref = None
+    if args.ref_streams:
+        with open(args.ref_streams) as f:
+            ref = json.load(f)
+    for tp in [int(x) for x in args.tp_list.split(",")]:
+        out = os.path.join(tempfile.gettempdir(), f"fxpr_streams_tp{tp}.json")
+        cmd = [sys.executable, "-m", "fxpr_vllm.e2e", "--preset", args.preset, "--prompts",
+               str(args.prompts), "--prompt-len", str(args.prompt_len), "--gen", str(args.gen),
+               "--tp", str(tp), "--out", out]
+        if args.model_dir:
+            cmd += ["--model-dir", args.model_dir]
+        r = subprocess.run(cmd, capture_output=True, text=True)
+        line = [ln for ln in r.stdout.splitlines() if ln.startswith("{")]
+        if r.returncode != 0 or not line:
+            rows.append({"tp": tp, "error": (r.stderr or r.stdout)[-2000:]})
+            continue
+        res = json.loads(line[-1])
+        with open(out) as f:
+            streams[tp] = json.load(f)
+        res["streams_sha256_16"] = streams_sha(streams[tp])
+        rows.append(res)
+        print(json.dumps(res), flush=True)
+    vals = list(streams.values()) + ([ref] if ref is not None else [])
+    summary = {"preset": args.preset, "tp_degrees": [r["tp"] for r in rows],
+               "identical_across_tp": bool(vals) and all(v == vals[0] for v in vals),
+               "reference_streams_sha256_16": streams_sha(ref) if ref is not None else None,
+               "runs": rows}
+    print(json.dumps(summary), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--preset", default="llama1b", choices=sorted(PRESETS))
@@ -136,7 +181,12 @@ def main():
     ap.add_argument("--tp", type=int, default=1)
     ap.add_argument("--batches", default="", help="comma list of batch sizes to compare")
     ap.add_argument("--out", default=None, help="write token streams (json) here")
+    ap.add_argument("--tp-list", default="", help="comma list of TP degrees, one process each")
+    ap.add_argument("--ref-streams", default=None, help="streams (json) every TP degree must match")
     args = ap.parse_args()
+    if args.tp_list:
+        _tp_list(args)
+        return
     d = make_llama_dir(args.model_dir or f"/tmp/fxpr_{args.preset}", args.preset)
     llm = make_llm(d, tp=args.tp, max_num_seqs=max(args.prompts, 1),
                    max_model_len=args.prompt_len + args.gen + 16)
@@ -154,7 +204,8 @@ def main():
     res = {"preset": args.preset, "tp": args.tp, "prompts": args.prompts,
            "prompt_len": args.prompt_len, "gen": args.gen,
            "decode_tok_s": round(args.prompts * (args.gen - 1) / decode_s, 2),
-           "total_s": round(t_all, 3), "prefill_s": round(t_prefill, 3)}
+           "total_s": round(t_all, 3), "prefill_s": round(t_prefill, 3),
+           "streams_sha256_16": streams_sha(out)}
     if args.batches:
         same = True
         for b in [int(x) for x in args.batches.split(",")]:
