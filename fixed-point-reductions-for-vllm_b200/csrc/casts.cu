@@ -137,85 +137,82 @@ __global__ void __launch_bounds__(256) fxp_sum_kernel(const T* __restrict__ x, i
   }
 }
 
-// Vectorised bf16 / fp32 variant: F2X by the magic-constant rounding, two
-// elements per packed FMA (x * 2^f is exact, so one rounding = RNE), integer
-// sums of the bit patterns. A thread whose elements all satisfy
-// |x| * 2^f < 2^22 (int16: < 32767.5, inside the clamp range) is exact on the
-// fast path; a thread with a larger, inf or NaN element recomputes its own
-// elements with the clamp-and-convert path. Both give the same bits.
+// Vectorised bf16 / fp32 variant: one warp per row (grid-stride over rows),
+// 16-byte loads eight deep per lane, F2X by the magic-constant rounding (two
+// elements per packed FMA; x * 2^f is exact, so one rounding = RNE), integer
+// sums of the bit patterns, warp-shuffle reduction. A lane whose elements all
+// satisfy |x| * 2^f < 2^22 (int16: < 32767.5, inside the clamp range) is
+// exact on the fast path; a lane with a larger, inf or NaN element recomputes
+// its own elements with the clamp-and-convert path. Same bits either way.
 template <int BITS, typename T>
-__global__ void __launch_bounds__(256) fxp_sum_magic_kernel(const T* __restrict__ x, int64_t cols,
-                                                            int64_t stride, float* __restrict__ out,
-                                                            int frac, float thr) {
+__global__ void __launch_bounds__(256) fxp_sum_magic_kernel(const T* __restrict__ x, int64_t rows,
+                                                            int64_t cols, int64_t stride,
+                                                            float* __restrict__ out, int frac,
+                                                            float thr) {
   constexpr int VEC = 16 / sizeof(T);
-  const int64_t row = blockIdx.x;
-  const T* xr = x + row * stride;
-  const uint4* xv = reinterpret_cast<const uint4*>(xr);
-  const int64_t nv = cols / VEC;
+  constexpr int DEPTH = 8;  // 16-byte loads in flight per lane
+  const int lane = threadIdx.x & 31;
+  const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
   const float scale = ldexpf(1.0f, frac);
   const float2 S2 = make_float2(scale, scale), C2 = make_float2(kMagic, kMagic);
-  long long acc = 0;
-  uint32_t m_u = 0, m_s = 0x80008000u;  // |x| bound of 16-bit elements (raw halves)
-  uint32_t m32 = 0;                     // |x| bound of fp32 elements (bit patterns)
-  auto take = [&](uint4 w) {
-    const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
-    uint32_t part = 0;
-    if constexpr (sizeof(T) == 2) {
-      m_u = __vimax3_u16x2(m_u, w.x, w.y);
-      m_u = __vimax3_u16x2(m_u, w.z, w.w);
-      m_s = (uint32_t)__vimax3_s16x2((int)m_s, (int)w.x, (int)w.y);
-      m_s = (uint32_t)__vimax3_s16x2((int)m_s, (int)w.z, (int)w.w);
+  for (int64_t row = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); row < rows;
+       row += warps) {
+    const T* xr = x + row * stride;
+    const uint4* xv = reinterpret_cast<const uint4*>(xr);
+    const int64_t nv = cols / VEC;
+    long long acc = 0;
+    uint32_t m_u = 0, m_s = 0x80008000u;  // |x| bound of 16-bit elements (raw halves)
+    uint32_t m32 = 0;                     // |x| bound of fp32 elements (bit patterns)
+    auto take = [&](uint4 w) {
+      const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+      uint32_t part = 0;
+      if constexpr (sizeof(T) == 2) {
+        m_u = __vimax3_u16x2(m_u, w.x, w.y);
+        m_u = __vimax3_u16x2(m_u, w.z, w.w);
+        m_s = (uint32_t)__vimax3_s16x2((int)m_s, (int)w.x, (int)w.y);
+        m_s = (uint32_t)__vimax3_s16x2((int)m_s, (int)w.z, (int)w.w);
 #pragma unroll
-      for (int k = 0; k < 4; ++k) {
-        const float2 f = make_float2(__uint_as_float(ws[k] << 16), __uint_as_float(ws[k] & 0xFFFF0000u));
-        const float2 r = fma2(f, S2, C2);
-        part += __float_as_uint(r.x) + __float_as_uint(r.y);
-      }
-      part -= (uint32_t)8 * (uint32_t)kMagicBits;
-    } else {
-      m32 = max(max(m32, ws[0] & 0x7FFFFFFFu), ws[1] & 0x7FFFFFFFu);
-      m32 = max(max(m32, ws[2] & 0x7FFFFFFFu), ws[3] & 0x7FFFFFFFu);
+        for (int k = 0; k < 4; ++k) {
+          const float2 f = make_float2(__uint_as_float(ws[k] << 16), __uint_as_float(ws[k] & 0xFFFF0000u));
+          const float2 r = fma2(f, S2, C2);
+          part += __float_as_uint(r.x) + __float_as_uint(r.y);
+        }
+        part -= (uint32_t)8 * (uint32_t)kMagicBits;
+      } else {
+        m32 = max(max(m32, ws[0] & 0x7FFFFFFFu), ws[1] & 0x7FFFFFFFu);
+        m32 = max(max(m32, ws[2] & 0x7FFFFFFFu), ws[3] & 0x7FFFFFFFu);
 #pragma unroll
-      for (int k = 0; k < 4; k += 2) {
-        const float2 r = fma2(make_float2(__uint_as_float(ws[k]), __uint_as_float(ws[k + 1])), S2, C2);
-        part += __float_as_uint(r.x) + __float_as_uint(r.y);
+        for (int k = 0; k < 4; k += 2) {
+          const float2 r = fma2(make_float2(__uint_as_float(ws[k]), __uint_as_float(ws[k + 1])), S2, C2);
+          part += __float_as_uint(r.x) + __float_as_uint(r.y);
+        }
+        part -= (uint32_t)4 * (uint32_t)kMagicBits;
       }
-      part -= (uint32_t)4 * (uint32_t)kMagicBits;
+      acc += (long long)(int32_t)part;  // |part| <= 8 * 2^22
+    };
+    int64_t i = lane;
+    for (; i + (DEPTH - 1) * 32 < nv; i += DEPTH * 32) {
+      uint4 t[DEPTH];
+#pragma unroll
+      for (int k = 0; k < DEPTH; ++k) t[k] = __ldcs(xv + i + k * 32);
+#pragma unroll
+      for (int k = 0; k < DEPTH; ++k) take(t[k]);
     }
-    acc += (long long)(int32_t)part;  // |part| <= 8 * 2^22
-  };
-  int64_t i = threadIdx.x;
-  for (; i + 3 * (int64_t)blockDim.x < nv; i += 4 * (int64_t)blockDim.x) {
-    uint4 t[4];
-#pragma unroll
-    for (int k = 0; k < 4; ++k) t[k] = __ldcs(xv + i + k * blockDim.x);
-#pragma unroll
-    for (int k = 0; k < 4; ++k) take(t[k]);
-  }
-  for (; i < nv; i += blockDim.x) take(__ldcs(xv + i));
-  float mx;
-  if constexpr (sizeof(T) == 2) {
-    const uint32_t pk = __vmaxu2(m_u & 0x7FFF7FFFu, m_s & 0x7FFF7FFFu);
-    mx = __uint_as_float(max(pk & 0xFFFFu, pk >> 16) << 16);
-  } else {
-    mx = __uint_as_float(m32);
-  }
-  if (!(mx < thr)) {  // this thread's vectors again, each element clamped alone
-    acc = 0;
-    for (int64_t v = threadIdx.x; v < nv; v += blockDim.x)
-      for (int e = 0; e < VEC; ++e) acc += (long long)f2x_f32<BITS>(to_f32(xr[v * VEC + e]), scale);
-  }
-  for (int64_t k = nv * VEC + threadIdx.x; k < cols; k += blockDim.x)
-    acc += (long long)f2x_f32<BITS>(to_f32(xr[k]), scale);
-  // integer block reduction (exact, order-free)
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
-  __shared__ long long red[32];
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  if (lane == 0) red[warp] = acc;
-  __syncthreads();
-  if (warp == 0) {
-    acc = (lane < (int)(blockDim.x >> 5)) ? red[lane] : 0;
+    for (; i < nv; i += 32) take(__ldcs(xv + i));
+    float mx;
+    if constexpr (sizeof(T) == 2) {
+      const uint32_t pk = __vmaxu2(m_u & 0x7FFF7FFFu, m_s & 0x7FFF7FFFu);
+      mx = __uint_as_float(max(pk & 0xFFFFu, pk >> 16) << 16);
+    } else {
+      mx = __uint_as_float(m32);
+    }
+    if (!(mx < thr)) {  // this lane's vectors again, each element clamped alone
+      acc = 0;
+      for (int64_t v = lane; v < nv; v += 32)
+        for (int e = 0; e < VEC; ++e) acc += (long long)f2x_f32<BITS>(to_f32(xr[v * VEC + e]), scale);
+    }
+    for (int64_t k = nv * VEC + lane; k < cols; k += 32)
+      acc += (long long)f2x_f32<BITS>(to_f32(xr[k]), scale);
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
     if (lane == 0) {
@@ -242,10 +239,16 @@ static int launch_fxp_sum(const void* x, int dtype, int64_t rows, int64_t cols, 
   // the clamp range), as an fp32 threshold on |x|
   const float thr = (float)ldexp(BITS == 16 ? 32767.5 : 4194304.0, -frac);
   if (aligned && frac <= 100 && (dtype == FXPR_BF16 || dtype == FXPR_F32)) {
+    // 8 rows (warps) per CTA, at most 16 CTAs per SM's worth of rows in one wave
+    int64_t g = cdiv(rows, 8);
+    const int64_t cap = (int64_t)num_sms() * 8;
+    if (g > cap) g = cap;
     if (dtype == FXPR_BF16)
-      fxp_sum_magic_kernel<BITS, __nv_bfloat16><<<grid, block, 0, st>>>((const __nv_bfloat16*)x, cols, stride, out, frac, thr);
+      fxp_sum_magic_kernel<BITS, __nv_bfloat16><<<(unsigned)g, 256, 0, st>>>(
+          (const __nv_bfloat16*)x, rows, cols, stride, out, frac, thr);
     else
-      fxp_sum_magic_kernel<BITS, float><<<grid, block, 0, st>>>((const float*)x, cols, stride, out, frac, thr);
+      fxp_sum_magic_kernel<BITS, float><<<(unsigned)g, 256, 0, st>>>((const float*)x, rows, cols,
+                                                                      stride, out, frac, thr);
     return check_launch("fxpr_fxp_sum");
   }
   switch (dtype) {

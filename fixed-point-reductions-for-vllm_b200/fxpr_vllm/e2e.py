@@ -49,12 +49,15 @@ def make_llama_dir(path: str, preset: str = "tiny", seed: int = 0) -> str:
         "bos_token_id": 1, "eos_token_id": 2, "attention_bias": False, "mlp_bias": False,
         **cfg,
     }
-    g = torch.Generator().manual_seed(seed)
+    # drawn on the GPU when there is one (seconds for 8B parameters instead of
+    # minutes on the host); the same seed gives the same weights on every run
+    dev = "cuda" if torch.cuda.is_available() else "cpu"
+    g = torch.Generator(device=dev).manual_seed(seed)
     H, L, I, V = cfg["hidden_size"], cfg["num_hidden_layers"], cfg["intermediate_size"], cfg["vocab_size"]
     nh, nkv, hd = cfg["num_attention_heads"], cfg["num_key_value_heads"], cfg["head_dim"]
 
     def rnd(*shape):
-        return (torch.randn(*shape, generator=g) * 0.02).to(torch.bfloat16)
+        return (torch.randn(*shape, generator=g, device=dev) * 0.02).to(torch.bfloat16).cpu()
 
     sd = {"model.embed_tokens.weight": rnd(V, H), "lm_head.weight": rnd(V, H),
           "model.norm.weight": torch.ones(H, dtype=torch.bfloat16)}
@@ -93,6 +96,9 @@ def make_llm(model_dir: str, tp: int = 1, max_num_seqs: int = 256, gpu_mem: floa
     # rendezvous on loopback: the host name of the box may not resolve
     os.environ.setdefault("VLLM_HOST_IP", "127.0.0.1")
     os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+    # greedy decoding needs no FlashInfer top-k/top-p sampler, whose first use
+    # JIT-compiles a module (minutes on a fresh machine)
+    os.environ.setdefault("VLLM_USE_FLASHINFER_SAMPLER", "0")
     from fxpr_vllm.register import register
 
     register()
@@ -152,6 +158,8 @@ def _tp_list(args) -> None:
                "--tp", str(tp), "--out", out]
         if args.model_dir:
             cmd += ["--model-dir", args.model_dir]
+        if args.eager:
+            cmd += ["--eager"]
         r = subprocess.run(cmd, capture_output=True, text=True)
         line = [ln for ln in r.stdout.splitlines() if ln.startswith("{")]
         if r.returncode != 0 or not line:
@@ -182,6 +190,7 @@ def main():
     ap.add_argument("--batches", default="", help="comma list of batch sizes to compare")
     ap.add_argument("--out", default=None, help="write token streams (json) here")
     ap.add_argument("--tp-list", default="", help="comma list of TP degrees, one process each")
+    ap.add_argument("--eager", action="store_true", help="no torch.compile / CUDA graphs")
     ap.add_argument("--ref-streams", default=None, help="streams (json) every TP degree must match")
     args = ap.parse_args()
     if args.tp_list:
@@ -189,7 +198,7 @@ def main():
         return
     d = make_llama_dir(args.model_dir or f"/tmp/fxpr_{args.preset}", args.preset)
     llm = make_llm(d, tp=args.tp, max_num_seqs=max(args.prompts, 1),
-                   max_model_len=args.prompt_len + args.gen + 16)
+                   max_model_len=args.prompt_len + args.gen + 16, enforce_eager=args.eager)
     ps = prompts(args.prompts, args.prompt_len, PRESETS[args.preset]["vocab_size"])
     generate(llm, ps[:2], 4)  # warm-up
     generate(llm, ps, 2)      # warm-up at full batch (prefix cache off, see make_llm)
@@ -203,7 +212,7 @@ def main():
     decode_s = max(t_all - t_prefill, 1e-9)
     res = {"preset": args.preset, "tp": args.tp, "prompts": args.prompts,
            "prompt_len": args.prompt_len, "gen": args.gen,
-           "decode_tok_s": round(args.prompts * (args.gen - 1) / decode_s, 2),
+           "eager": args.eager, "decode_tok_s": round(args.prompts * (args.gen - 1) / decode_s, 2),
            "total_s": round(t_all, 3), "prefill_s": round(t_prefill, 3),
            "streams_sha256_16": streams_sha(out)}
     if args.batches:
