@@ -45,7 +45,7 @@ constexpr int PG = 16;     // keys per page tile
 constexpr int RP = 4;      // query rows per item (the GQA group)
 constexpr int TPK = 8;     // lanes sharing one key in the scores kernel
 #ifndef FXPR_DQ_STAGES
-#define FXPR_DQ_STAGES 3
+#define FXPR_DQ_STAGES 2
 #endif
 constexpr int S = FXPR_DQ_STAGES;  // page buffers per warp
 constexpr int MAX_REQ = 4096;

@@ -457,9 +457,6 @@ __global__ void __launch_bounds__(THREADS, MinBlocks<BITS>::v) gemm_kernel(Param
 // integer. No operand is scaled.
 // ---------------------------------------------------------------------------
 constexpr int KC_LD = BK + 4;  // fp32 row pitch of the staged tiles
-#ifndef FXPR_GEMM_KC_REUSE
-#define FXPR_GEMM_KC_REUSE 0
-#endif
 
 template <int BM, int BITS, typename T>
 __global__ void __launch_bounds__(THREADS, BM == 16 ? 4 : 2) gemm_kc_kernel(Params p) {
@@ -604,19 +601,6 @@ __global__ void __launch_bounds__(THREADS, BM == 16 ? 4 : 2) gemm_kc_kernel(Para
         for (int i = 0; i < TM; ++i) {
           const float4 av = *reinterpret_cast<const float4*>(Ab + i * KC_LD + kk);
           const float2 a0 = make_float2(av.x, av.y), a1 = make_float2(av.z, av.w);
-#if FXPR_GEMM_KC_REUSE
-          float2 r0[TN], r1[TN];
-#pragma unroll
-          for (int j = 0; j < TN; ++j) r0[j] = fma2(a0, make_float2(bv[j].x, bv[j].y), CF2);
-#pragma unroll
-          for (int j = 0; j < TN; ++j) r1[j] = fma2(a1, make_float2(bv[j].z, bv[j].w), CF2);
-#pragma unroll
-          for (int j = 0; j < TN; ++j)
-            acc[i][j] += __float_as_uint(r0[j].x) + __float_as_uint(r0[j].y);
-#pragma unroll
-          for (int j = 0; j < TN; ++j)
-            acc[i][j] += __float_as_uint(r1[j].x) + __float_as_uint(r1[j].y);
-#else
 #pragma unroll
           for (int j = 0; j < TN; ++j) {
             const float2 r0 = fma2(a0, make_float2(bv[j].x, bv[j].y), CF2);
@@ -624,7 +608,6 @@ __global__ void __launch_bounds__(THREADS, BM == 16 ? 4 : 2) gemm_kc_kernel(Para
             acc[i][j] += __float_as_uint(r0.x) + __float_as_uint(r0.y);
             acc[i][j] += __float_as_uint(r1.x) + __float_as_uint(r1.y);
           }
-#endif
         }
       }
 #pragma unroll
