@@ -618,7 +618,10 @@ def main():
                     k: round(v / statistics.median(per[k]), 2) for k, v in dev_base["ms_per_op"].items()}},
             "tp_layer": tp,
             "e2e": {"value": round(e2e_val, 3), "unit": "GB/s", "h2d_bytes_per_step": h2d,
-                    "d2h_bytes_per_step": d2h},
+                    "d2h_bytes_per_step": d2h,
+                    # share of the end-to-end step spent in the kernels (the rest:
+                    # PCIe copies of the 2.6 GB KV pool and the outputs)
+                    "device_share": round(ms_step / e2e_ms, 4)},
             "gpu_launches": 5 * args.steps,  # gemm, rms_norm, fxp_sum, 2 x attention
             "clocks": clk.summary(),
         }
