@@ -49,6 +49,8 @@ constexpr int TPK = 8;     // lanes sharing one key in the scores kernel
 #endif
 constexpr int S = FXPR_DQ_STAGES;  // page buffers per warp
 constexpr int MAX_REQ = 4096;
+constexpr int kRedGroup = 72;             // words per key group in the transpose buffer
+constexpr int kRedWords = 4 * kRedGroup;  // per warp
 
 // error bits written to the workspace's first word
 constexpr uint32_t kErrContextCut = 1u;  // a context longer than max_seq_len was cut
@@ -185,6 +187,9 @@ __device__ __forceinline__ uint32_t lds32(uint32_t a) {
   uint32_t v;
   asm volatile("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(a));
   return v;
+}
+__device__ __forceinline__ void sts32(uint32_t a, uint32_t v) {
+  asm volatile("st.shared.u32 [%0], %1;" ::"r"(a), "r"(v) : "memory");
 }
 __device__ __forceinline__ void sts64f(uint32_t a, float x, float y) {
   asm volatile("st.shared.v2.f32 [%0], {%1, %2};" ::"r"(a), "f"(x), "f"(y) : "memory");
@@ -323,7 +328,10 @@ dq_scores_kernel(const __grid_constant__ CUtensorMap kmap, const DqParams p) {
   unsigned char* stage0 = smem + warp * (S * PAGEB);
   const uint32_t stage0_a = tma::smem_addr(stage0);
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + W * S * PAGEB) + warp * S;
-  int* pre = reinterpret_cast<int*>(smem + W * S * PAGEB + W * S * 8);
+  // per warp: the partial-dot transpose buffer, [key group][value][lane] with
+  // a 72-word group pitch (conflict-free writes), then the page prefix
+  uint32_t* red = reinterpret_cast<uint32_t*>(smem + W * S * PAGEB + W * S * 8) + warp * kRedWords;
+  int* pre = reinterpret_cast<int*>(smem + W * S * PAGEB + W * S * 8 + W * kRedWords * 4);
 
   build_prefix(p, pre);
   const int64_t T_ = pre[p.R];
@@ -447,8 +455,15 @@ dq_scores_kernel(const __grid_constant__ CUtensorMap kmap, const DqParams p) {
 #pragma unroll
           for (int row = 0; row < RP; ++row)
             v[mm * RP + row] = acc[mm][row] - (uint32_t)DPT * (uint32_t)kMagicBits;
-        reduce_scatter8_u32(v, kq);
-        dot = (long long)(int32_t)v[0];  // |fast-path dot| < 2^29
+        // sum over the 8 lanes of the key group, value kq to lane kq: each
+        // lane stores its 8 partials as [value][lane] and reads its value's 8
+        const uint32_t wbase = tma::smem_addr(red) + (kg * kRedGroup) * 4;
+#pragma unroll
+        for (int k = 0; k < 8; ++k) sts32(wbase + (k * 8 + kq) * 4, v[k]);
+        __syncwarp();
+        const uint4 a = lds128(wbase + (kq * 8) * 4), b = lds128(wbase + (kq * 8 + 4) * 4);
+        __syncwarp();  // the buffer is rewritten by the next step
+        dot = (long long)(int32_t)((a.x + a.y + a.z) + (a.w + b.x + b.y) + (b.z + b.w));  // |dot| < 2^29
       } else {
         Dots8 ex = exact_dots<D, BITS, T>(qbase, p.q_sh, kt, st * 8 + kg, kq, scale);
         reduce_scatter8_u64(ex.v, kq);
@@ -761,7 +776,7 @@ dq_pv_kernel(const __grid_constant__ CUtensorMap vmap, const DqParams p) {
 // ---------------------------------------------------------------------------
 template <int D>
 static size_t smem1(int R) {
-  return (size_t)W * S * Geo<D>::PAGEB + W * S * 8 + (size_t)(R + 1) * 4;
+  return (size_t)W * S * Geo<D>::PAGEB + W * S * 8 + (size_t)W * kRedWords * 4 + (size_t)(R + 1) * 4;
 }
 template <int D>
 static size_t smem2(int R) {
