@@ -33,7 +33,7 @@ Integer arguments are compiled as i32 and pointers without alignment hints
 (the JIT would add divisibility hints; they change address arithmetic, not
 the floating-point operations).
 
-    python oracle/build_ref.py [REFERENCE_ROOT]      # default /root/reference
+    python oracle/build_ref.py [REFERENCE_ROOT]   # default: $FXPR_REFERENCE_ROOT or DEFAULT_REF
 """
 
 from __future__ import annotations
@@ -45,7 +45,7 @@ import sys
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 OUT = os.path.join(HERE, "_ref")
-DEFAULT_REF = "/root/reference"
+DEFAULT_REF = os.environ.get("FXPR_REFERENCE_ROOT", "/root/reference")
 RCP_LN2 = 1.4426950408889634
 
 
